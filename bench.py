@@ -1,0 +1,422 @@
+"""Benchmark of the Co-ALiBi hot path (forward + backward) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config cfg2|cfg3|cfg4] [--scaling weak|strong]
+
+One step = co_alibi_attention(q, k, v, causal) forward and backward over one
+batch of the named configuration (default cfg2: B=8, H=16, S=4096, D=128, fp16,
+causal -- the reference README's bench shape at the baseline batch).  Inputs are
+seeded synthetic N(0, std) tensors drawn on the CPU and copied to the GPU; all
+of them (512 MiB at cfg2) exceed the 126 MB L2, so no flush is needed between
+steps.  N>1 runs one process per GPU under torchrun; every rank runs its own
+(b, h) units with no collective on the data path ("weak": each rank holds a full
+batch; "strong": the batch's B*Hkv units are split across ranks).  Time is taken
+with CUDA events on the launching stream, between a barrier and a synchronize,
+and the maximum over ranks is reported.
+
+Prints ONE JSON line (rank 0).  ``--impl reference`` times the reference
+algorithm's CPU path (the oracle restatement of model.py, on all host cores)
+on a bounded sample of the same workload and prints the same metric.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "co-alibi_b200"))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+CONFIGS = {
+    # name: B, Hq, Hkv, S, D, dtype, causal, input std, fwd_only
+    "cfg2": (8, 16, 16, 4096, 128, torch.float16, True, 1.0, False),
+    "cfg3": (4, 32, 8, 8192, 128, torch.bfloat16, True, 1.0, False),
+    "cfg4": (16, 12, 12, 2048, 64, torch.float16, False, 0.5, True),
+}
+
+# Per-launch DRAM traffic (read + write bytes) of each kernel at cfg2 from one
+# ncu capture (profiles/ncu_cfg2_*.txt); None where not captured yet.
+NCU_TRAFFIC_CFG2 = {"fwd": None, "bwd_a": None, "bwd_b": None, "bwd_delta": None}
+
+
+def visible(S, causal):
+    return S * (S + 1) // 2 if causal else S * S
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("bf16_tflops"), d.get("bf16_tflops_sustained"), d.get("hbm_gbs"), "measured"
+    except Exception:
+        return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks sampler (nvidia-smi during the timed region)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.idx)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        mhz, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                mhz.append(float(f[1]))
+                maxes.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not mhz:
+            return None
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+def physical_gpu_index(local_rank):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        parts = [p.strip() for p in vis.split(",") if p.strip()]
+        if local_rank < len(parts) and parts[local_rank].isdigit():
+            return int(parts[local_rank])
+    return local_rank
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the oracle restatement of the reference's model.py
+# ---------------------------------------------------------------------------
+def cpu_sample_tflops(cfg, rows, reps, threads=None):
+    """Time fwd+bwd of the oracle (model.py maths, fp32, all host threads) on the
+    last `rows` query rows of one (b, h) slice of the config.  Returns (TFLOP/s,
+    seconds per sample, threads, description)."""
+    from oracle import coalibi_oracle as orc
+    B, Hq, Hkv, S, D, dtype, causal, std, fwd_only = cfg
+    if threads:
+        torch.set_num_threads(threads)
+    nthreads = torch.get_num_threads()
+    g = torch.Generator().manual_seed(1)
+    q = (torch.randn(1, 1, rows, D, generator=g) * std).to(dtype)
+    k = (torch.randn(1, 1, S, D, generator=g) * std).to(dtype)
+    v = (torch.randn(1, 1, S, D, generator=g) * std).to(dtype)
+    do = torch.randn(1, 1, rows, D, generator=g).to(dtype)
+    sl = orc.api_slopes(Hq, 8.0, dtype)[:1]
+    off = S - rows
+    f, b = orc.algorithmic_flops(1, 1, rows, S, D, causal, q_offset=off)
+    flops = f if fwd_only else f + b
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        if fwd_only:
+            orc.forward(q, k, v, sl, causal, None, torch.float32, q_offset=off)
+        else:
+            orc.forward_backward(q, k, v, do, sl, causal, None, torch.float32, q_offset=off)
+        ts.append(time.perf_counter() - t0)
+    t = statistics.median(ts)
+    desc = (f"oracle (model.py maths) fp32 {'fwd' if fwd_only else 'fwd+bwd'} on one (b,h) slice, "
+            f"query rows {off}..{S - 1} of S={S}, D={D}, median of {reps}")
+    return flops / t / 1e12, t, nthreads, desc
+
+
+def run_reference_arm(args, cfg, rank):
+    if rank != 0:
+        return
+    B, Hq, Hkv, S, D, dtype, causal, std, fwd_only = cfg
+    # size each step so that warmup + steps fit in about two minutes
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    rows = S
+    _, t, _, _ = cpu_sample_tflops(cfg, min(S, 512), 1)
+    per_row = t / min(S, 512)
+    while rows > 64 and rows * per_row * 1.5 > budget:
+        rows //= 2
+    from oracle import coalibi_oracle as orc
+    tfl, tsec, nthreads, desc = cpu_sample_tflops(cfg, rows, args.warmup + args.steps)
+    ms = tsec * 1e3
+    line = {
+        "impl": "reference", "metric": metric_name(args.config), "value": round(tfl, 6), "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": config_dict(args, cfg),
+        "cpu_baseline": {"value": round(tfl, 6), "unit": "TFLOP/s", "cores": nthreads, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": round(tfl, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference arm: the reference's own CPU path (model.py maths) restated in oracle/, "
+                "timed on the host cores; the reference's Triton GPU kernels are not installable here",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def metric_name(config):
+    return {"cfg2": "fwd+bwd TFLOP/s (algorithmic causal), B8 H16 S4096 D128 fp16 causal",
+            "cfg3": "fwd+bwd TFLOP/s (algorithmic causal), GQA B4 Hq32 Hkv8 S8192 D128 bf16 causal",
+            "cfg4": "fwd TFLOP/s, B16 H12 S2048 D64 fp16 non-causal"}[config]
+
+
+def config_dict(args, cfg):
+    B, Hq, Hkv, S, D, dtype, causal, std, fwd_only = cfg
+    per_rank_B = B if args.scaling == "weak" else B
+    return {"workload": f"{args.config}: co_alibi_attention {'fwd' if fwd_only else 'fwd+bwd'} B={B} Hq={Hq} "
+                        f"Hkv={Hkv} S={S} D={D} {str(dtype).split('.')[-1]} "
+                        f"{'causal' if causal else 'non-causal'}",
+            "global_batch": B * (args.gpus if args.scaling == "weak" else 1), "seq_len": S,
+            "heads": Hq, "kv_heads": Hkv, "head_dim": D, "per_rank_batch": per_rank_B,
+            "parallelism": f"(b,h)-shards x{args.gpus}, no data-path collective",
+            "l2": "inputs (4 x B*H*S*D*2 bytes) exceed the 126 MB L2; no flush needed"}
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    cfg = CONFIGS[args.config]
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference_arm(args, cfg, rank)
+        return
+
+    import datetime
+    import torch.distributed as dist
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    import co_alibi_attn
+    from co_alibi_attn import co_alibi_attention
+    import co_alibi_attn.co_alibi_attn as impl
+
+    B, Hq, Hkv, S, D, dtype, causal, std, fwd_only = cfg
+    if args.scaling == "strong" and world > 1:
+        # split the batch's B*Hkv units; each rank keeps whole batch rows when possible
+        assert B % world == 0 or (B * Hkv) % world == 0
+        B_r = B // world if B % world == 0 else B
+        Hkv_r = Hkv if B % world == 0 else Hkv // world
+        Hq_r = Hq if B % world == 0 else Hq // world
+    else:
+        B_r, Hq_r, Hkv_r = B, Hq, Hkv
+
+    g = torch.Generator().manual_seed(1000 + rank)
+    q_h = (torch.randn(B_r, Hq_r, S, D, generator=g) * std).to(dtype).pin_memory()
+    k_h = (torch.randn(B_r, Hkv_r, S, D, generator=g) * std).to(dtype).pin_memory()
+    v_h = (torch.randn(B_r, Hkv_r, S, D, generator=g) * std).to(dtype).pin_memory()
+    do_h = torch.randn(B_r, Hq_r, S, D, generator=g).to(dtype).pin_memory()
+    q = q_h.to(dev).requires_grad_(not fwd_only)
+    k = k_h.to(dev).requires_grad_(not fwd_only)
+    v = v_h.to(dev).requires_grad_(not fwd_only)
+    do = do_h.to(dev)
+
+    E = visible(S, causal) * B_r * Hq_r
+    flops_fwd = 4.0 * D * E
+    flops_step = flops_fwd if fwd_only else 14.0 * D * E
+    kernels_per_step = 1 if fwd_only else 4
+
+    def step():
+        if fwd_only:
+            with torch.no_grad():
+                co_alibi_attention(q, k, v, causal=causal)
+        else:
+            o = co_alibi_attention(q, k, v, causal=causal)
+            o.backward(do)
+            q.grad = k.grad = v.grad = None
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    assert co_alibi_attn.device_status(reset=True) == 0, "kernel-side error during warmup"
+
+    # ---------------- timed region (also records per-kernel events)
+    impl.kernel_events = {}
+    sampler = ClockSampler(physical_gpu_index(local_rank))
+    sampler.start()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    rec = impl.kernel_events
+    impl.kernel_events = None
+    ms = e0.elapsed_time(e1) / args.steps
+    kern_ms = {name: statistics.mean(a.elapsed_time(b) for a, b in pairs) for name, pairs in rec.items()}
+    status = co_alibi_attn.device_status(reset=True)
+
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = t.item()
+    value = world * flops_step / (ms_max * 1e-3) / 1e12
+
+    # ---------------- forward-only timing (the metric's fwd half)
+    fwd_ms = kern_ms.get("fwd")
+    # ---------------- e2e: pinned host inputs -> device -> API -> host outputs
+    outs_h = [torch.empty_like(q_h).pin_memory()]
+    if not fwd_only:
+        outs_h += [torch.empty_like(q_h).pin_memory(), torch.empty_like(k_h).pin_memory(),
+                   torch.empty_like(v_h).pin_memory()]
+    qd = torch.empty_like(q)
+    kd = torch.empty_like(k)
+    vd = torch.empty_like(v)
+    dod = torch.empty_like(do)
+
+    def e2e_step():
+        with torch.no_grad():
+            qd.copy_(q_h, non_blocking=True)
+            kd.copy_(k_h, non_blocking=True)
+            vd.copy_(v_h, non_blocking=True)
+            if not fwd_only:
+                dod.copy_(do_h, non_blocking=True)
+        if fwd_only:
+            with torch.no_grad():
+                o = co_alibi_attention(qd, kd, vd, causal=causal)
+            outs_h[0].copy_(o, non_blocking=True)
+        else:
+            qd.requires_grad_(True), kd.requires_grad_(True), vd.requires_grad_(True)
+            o = co_alibi_attention(qd, kd, vd, causal=causal)
+            o.backward(dod)
+            outs_h[0].copy_(o.detach(), non_blocking=True)
+            outs_h[1].copy_(qd.grad, non_blocking=True)
+            outs_h[2].copy_(kd.grad, non_blocking=True)
+            outs_h[3].copy_(vd.grad, non_blocking=True)
+            qd.grad = kd.grad = vd.grad = None
+            qd.requires_grad_(False), kd.requires_grad_(False), vd.requires_grad_(False)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    f1.record()
+    torch.cuda.synchronize()
+    e2e_ms = f0.elapsed_time(f1) / args.e2e_steps
+    t = torch.tensor([e2e_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = t.item()
+    h2d = sum(x.numel() * x.element_size() for x in ([q_h, k_h, v_h] + ([] if fwd_only else [do_h])))
+    d2h = sum(x.numel() * x.element_size() for x in outs_h)
+
+    # ---------------- roofline of the dominant kernel
+    burst, sustained, hbm, peak_src = load_peaks()
+    per_kernel_flops = {"fwd": 4.0 * D * E, "bwd_a": 6.0 * D * E, "bwd_b": 8.0 * D * E,
+                        "bwd_delta": 0.0}
+    per_kernel_mufu = {"fwd": 3.0 * E, "bwd_a": 3.0 * E, "bwd_b": 3.0 * E, "bwd_delta": 0.0}
+    dom = max(kern_ms, key=kern_ms.get)
+    ach = per_kernel_flops[dom] / (kern_ms[dom] * 1e-3) / 1e12
+    sm_mhz = clocks["sm_mhz"] if clocks else 1965.0
+    kernels = {}
+    for name, kms in kern_ms.items():
+        d = {"ms": round(kms, 4), "share": round(kms / ms, 4)}
+        if per_kernel_flops[name]:
+            d["tflops"] = round(per_kernel_flops[name] / (kms * 1e-3) / 1e12, 2)
+            d["mufu_frac"] = round(per_kernel_mufu[name] / (16 * 148 * sm_mhz * 1e6 * kms * 1e-3), 4)
+        kernels[name] = d
+    roof = {"bound": "tensor", "kernel": dom, "achieved": round(ach, 2), "peak": burst, "unit": "TFLOP/s",
+            "frac": round(ach / burst, 4), "peak_source": f"{peak_src} bf16_tflops (burst)",
+            "traffic": NCU_TRAFFIC_CFG2.get(dom) if args.config == "cfg2" and args.scaling == "weak" else None,
+            "flops_per_launch": per_kernel_flops[dom],
+            "note": "algorithmic FLOPs on causal-visible scores of the kernel's GEMMs "
+                    "(fwd 4D, pass A 6D, pass B 8D per score) / mean CUDA-event duration in the timed region; "
+                    "second roofline: mufu_frac = 3 MUFU ops per score / (16 ops/clk/SM x 148 SMs x sampled clock)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tfl, tsec, nth, desc = cpu_sample_tflops(cfg, S, 3)
+        cpu = {"value": round(tfl, 6), "unit": "TFLOP/s", "cores": nth, "kind": "port", "sample": desc,
+               "seconds_per_sample": round(tsec, 3)}
+
+    if rank == 0:
+        line = {
+            "metric": metric_name(args.config), "value": round(value, 3), "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4),
+            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
+            "dtype": str(dtype).split(".")[-1].replace("float16", "fp16").replace("bfloat16", "bf16"),
+            "data": "synthetic", "config": config_dict(args, cfg),
+            "fwd_ms": round(fwd_ms, 4) if fwd_ms else None,
+            "fwd_tflops": round(flops_fwd / (fwd_ms * 1e-3) / 1e12, 3) if fwd_ms else None,
+            "fwd_pct_of_tensor_peak_spec2250": round(100 * flops_fwd / (fwd_ms * 1e-3) / 2.25e15, 2) if fwd_ms else None,
+            "fwd_bwd_pct_of_tensor_peak_spec2250": round(100 * value / world / 2250.0, 2),
+            "fwd_bwd_tflops_reference_convention": round(
+                world * (12.0 * D * S * S * B_r * Hq_r if not fwd_only else 4.0 * D * S * S * B_r * Hq_r)
+                / (ms_max * 1e-3) / 1e12, 3),
+            "kernels": kernels, "roofline": roof, "cpu_baseline": cpu,
+            "e2e": {"value": round(world * flops_step / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+                    "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": kernels_per_step * args.steps, "clocks": clocks, "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,876 @@
+// Co-ALiBi attention backward for sm_100a: three kernels, no atomics, no
+// O(S^2) scratch, deterministic.
+//
+// With p = scale q.k, s = sigmoid(p), z_ij = sum_{t>=j} s_it, a = p - slope z,
+// P = exp(a - lse), the gradient of the penalised logits is
+//   dA_ij = P_ij (dO_i.v_j - delta_i),        delta_i = dO_i . O_i
+//   dp_ij = dA_ij - slope s_ij (1 - s_ij) c_ij, c_ij = sum_{t<=j} dA_it
+//   dQ = scale dp K,  dK = scale dp^T Q,  dV = P^T dO
+// (model.py:61-76 with the slope of co_alibi_attn/co_alibi_bwd_kernel.py:133).
+// z and c are running sums along the key axis of each query row, so a
+// key-major kernel cannot form them on its own.  The split is:
+//
+//  1. delta pre-pass: delta_i = dO_i . O_i (one warp per row).
+//  2. pass A, query-major (one CTA per 128-row query tile, key tiles left to
+//     right): recomputes S = Q K^T and dS = dO V^T into TMEM, runs the two
+//     scans in registers (one thread per row), accumulates dQ += dp K in TMEM,
+//     and records at every 64-key boundary the pair (z suffix, c prefix) of
+//     each row -- 8 bytes per (row, 64 keys).
+//  3. pass B, key-major (one CTA per block of keys of one kv head): for every
+//     query head of the GQA group and every query tile that sees the block it
+//     recomputes S and dS, restarts both scans from pass A's carries, writes
+//     P and dp to shared memory and accumulates dV += P^T dO and dK += dp^T Q
+//     in TMEM.  The GQA group sum therefore happens in TMEM.
+//
+// D = 128 uses 64-key blocks in pass B with transposed accumulators
+// (dV^T = dO^T P, M = D); D = 64 uses 128-key blocks (dV = P^T dO, M = keys).
+// Both keep every MMA at M = 128.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include "coalibi.h"
+#include "sm100.cuh"
+#include "fwd.cuh"
+
+namespace coalibi {
+
+struct BwdWorkspace {
+  size_t delta_off, carry_off, total;
+};
+
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// delta: float [B*Hq][sq_pad];  carry: float2 [B*Hq][n_kb64][sq_pad]
+inline BwdWorkspace bwd_workspace_layout(int B, int Hq, int Sq, int Skv) {
+  const size_t sq_pad = (size_t)((Sq + 127) / 128) * 128;
+  const size_t nkb = (size_t)((Skv + 63) / 64);
+  BwdWorkspace w;
+  w.delta_off = 0;
+  w.carry_off = align256((size_t)B * Hq * sq_pad * 4);
+  w.total = w.carry_off + align256((size_t)B * Hq * nkb * sq_pad * 8);
+  return w;
+}
+
+struct BwdParams {
+  const void* o;
+  const void* dout;
+  const float* lse;
+  const float* rowsig;
+  const void* slopes;
+  void* dq;
+  void* dk;
+  void* dv;
+  float* delta;
+  float2* carry;
+  int B, Hq, Hkv, Sq, Skv;
+  int slopes_dtype;
+  int causal;
+  float sm_scale;
+  int* status;
+  unsigned long long timeout_ns;
+  int n_qtiles;   // ceil(Sq / 128)
+  int n_kvtiles;  // ceil(Skv / 128)
+  int n_kb64;     // ceil(Skv / 64)
+  int n_blocks;   // pass-B key blocks: ceil(Skv / KB)
+  int sq_pad;
+};
+
+// ---------------------------------------------------------------------------
+// 1. delta pre-pass
+// ---------------------------------------------------------------------------
+template <int D, bool BF16>
+__global__ void __launch_bounds__(256) coalibi_bwd_delta_kernel(const BwdParams p) {
+  const long long nrows = (long long)p.B * p.Hq * p.sq_pad;
+  const long long rg = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (rg >= nrows) return;
+  const int lane = threadIdx.x & 31;
+  const int bh = (int)(rg / p.sq_pad);
+  const int row = (int)(rg - (long long)bh * p.sq_pad);
+  float acc = 0.f;
+  if (row < p.Sq) {
+    const size_t base = ((size_t)bh * p.Sq + row) * D;
+    if (D == 128) {
+      const uint2 a = reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.o) + base)[lane];
+      const uint2 b = reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.dout) + base)[lane];
+      const float2 a0 = unpack2<BF16>(a.x), a1 = unpack2<BF16>(a.y);
+      const float2 b0 = unpack2<BF16>(b.x), b1 = unpack2<BF16>(b.y);
+      acc = a0.x * b0.x + a0.y * b0.y + a1.x * b1.x + a1.y * b1.y;
+    } else {
+      const uint32_t a = reinterpret_cast<const uint32_t*>(static_cast<const uint16_t*>(p.o) + base)[lane];
+      const uint32_t b = reinterpret_cast<const uint32_t*>(static_cast<const uint16_t*>(p.dout) + base)[lane];
+      const float2 a0 = unpack2<BF16>(a), b0 = unpack2<BF16>(b);
+      acc = a0.x * b0.x + a0.y * b0.y;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) p.delta[rg] = acc;
+}
+
+// ---------------------------------------------------------------------------
+// Shared per-key maths of passes A and B: one 32-key chunk of a row, keys left
+// to right.  zs = suffix sum of sigmoids from the current key on (inclusive),
+// cacc = inclusive prefix of dA.  Writes 16 packed dp pairs and, if P_OUT, 16
+// packed P pairs.  Keys >= lim are masked.
+// ---------------------------------------------------------------------------
+template <bool MASK, bool BF16, bool P_OUT>
+__device__ __forceinline__ void bwd_chunk(const uint32_t* sreg, const uint32_t* dsreg, int key0, int lim,
+                                          float c_sig, float c_a, float slope, float slope2, float lse2,
+                                          float delta, float& zs, float& cacc, uint32_t* dp_out,
+                                          uint32_t* p_out) {
+#pragma unroll
+  for (int j2 = 0; j2 < 16; ++j2) {
+    float dpv[2], pv[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int j = 2 * j2 + u;
+      const float x = __uint_as_float(sreg[j]);
+      const float y = __uint_as_float(dsreg[j]);
+      float sg = sigmoid_from_neg_log2(x * c_sig);
+      const bool valid = !MASK || (key0 + j < lim);
+      if (!valid) sg = 0.f;
+      const float a2 = fmaf(-slope2, zs, x * c_a);
+      float P = ex2_approx(a2 - lse2);
+      if (!valid) P = 0.f;
+      const float dA = P * (y - delta);
+      cacc += dA;
+      const float sp = fmaf(-sg, sg, sg);  // s (1 - s)
+      dpv[u] = fmaf(-slope * sp, cacc, dA);
+      pv[u] = P;
+      zs -= sg;
+    }
+    dp_out[j2] = pack2<BF16>(dpv[0], dpv[1]);
+    if (P_OUT) p_out[j2] = pack2<BF16>(pv[0], pv[1]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 2. pass A: dQ and the per-64-key carries
+// ---------------------------------------------------------------------------
+template <int D>
+struct BwdALayout {
+  static constexpr int BM = 128, BN = 128;
+  static constexpr int KS = 2, VS = 2;
+  static constexpr int BOX = 128 * 128;
+  static constexpr int TILE = BN * D * 2;
+  static constexpr int QB = BM * D * 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_DO = QB;
+  static constexpr int OFF_K = 2 * QB;
+  static constexpr int OFF_V = OFF_K + KS * TILE;
+  static constexpr int OFF_BAR = OFF_V + VS * TILE;
+  static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 1 + 1 + 2 + 1 + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int BYTES = OFF_MISC + 16;
+  static constexpr int ALLOC = BYTES + 1024;
+  static constexpr uint32_t TM_S = 0, TM_DS = 128, TM_DQ = 256, TM_DP = 256 + D, TM_COLS = 512;
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(192, 1)
+    coalibi_bwd_a_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                         const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                         const BwdParams p) {
+  using L = BwdALayout<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + L::OFF_Q;
+  uint8_t* sDO = smem + L::OFF_DO;
+  uint8_t* sK = smem + L::OFF_K;
+  uint8_t* sV = smem + L::OFF_V;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + L::KS;
+  uint64_t* v_full = k_empty + L::KS;
+  uint64_t* v_empty = v_full + L::VS;
+  uint64_t* s_full = v_empty + L::VS;
+  uint64_t* s_free = s_full + 1;
+  uint64_t* dp_full = s_free + 1;
+  uint64_t* dq_done = dp_full + 2;
+  uint64_t* mma_idle = dq_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int BH = p.B * p.Hq;
+  int bh, m;
+  decode_tile(blockIdx.x, BH, p.n_qtiles, bh, m);
+  const int b = bh / p.Hq;
+  const int h = bh - b * p.Hq;
+  const int zkv = b * p.Hkv + h / (p.Hq / p.Hkv);
+  const int last = p.causal ? min(p.n_kvtiles - 1, (m * L::BM + L::BM - 1) / L::BN) : p.n_kvtiles - 1;
+  const int T = last + 1;
+  CtaGuard g{abort_flag, p.status, p.timeout_ns};
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < L::KS; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < L::VS; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 128);
+    mbar_init(&dp_full[0], 128);
+    mbar_init(&dp_full[1], 128);
+    mbar_init(dq_done, 1);
+    mbar_init(mma_idle, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, L::TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmDO);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(q_full, 2 * L::QB);
+#pragma unroll
+      for (int bx = 0; bx < D / 64; ++bx) {
+        tma_load_3d(sQ + bx * L::BOX, &tmQ, q_full, bx * 64, m * L::BM, bh);
+        tma_load_3d(sDO + bx * L::BOX, &tmDO, q_full, bx * 64, m * L::BM, bh);
+      }
+      int nk = 0, nv = 0;
+      for (int t = 0; t < T; ++t) {
+        const int ks = t % L::KS;
+        if (!mbar_wait(&k_empty[ks], ((t / L::KS) & 1) ^ 1, g)) break;
+        mbar_arrive_expect_tx(&k_full[ks], L::TILE);
+#pragma unroll
+        for (int bx = 0; bx < D / 64; ++bx)
+          tma_load_3d(sK + ks * L::TILE + bx * L::BOX, &tmK, &k_full[ks], bx * 64, t * L::BN, zkv);
+        ++nk;
+        const int vs = t % L::VS;
+        if (!mbar_wait(&v_empty[vs], ((t / L::VS) & 1) ^ 1, g)) break;
+        mbar_arrive_expect_tx(&v_full[vs], L::TILE);
+#pragma unroll
+        for (int bx = 0; bx < D / 64; ++bx)
+          tma_load_3d(sV + vs * L::TILE + bx * L::BOX, &tmV, &v_full[vs], bx * 64, t * L::BN, zkv);
+        ++nv;
+      }
+      mbar_drain(q_full, 0, g.timeout_ns);
+      for (int s = 0; s < L::KS; ++s) {
+        const int uses = (nk > s) ? (nk - 1 - s) / L::KS + 1 : 0;
+        if (uses > 0) mbar_drain(&k_full[s], (uses - 1) & 1, g.timeout_ns);
+      }
+      for (int s = 0; s < L::VS; ++s) {
+        const int uses = (nv > s) ? (nv - 1 - s) / L::VS + 1 : 0;
+        if (uses > 0) mbar_drain(&v_full[s], (uses - 1) & 1, g.timeout_ns);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      constexpr uint32_t idS = make_idesc_f16(BF16, 128, L::BN, false, false);
+      constexpr uint32_t idQ = make_idesc_f16(BF16, 128, D, false, true);
+      const uint32_t q_addr = smem_u32(sQ), do_addr = smem_u32(sDO);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      auto issue_SdS = [&](int t) -> bool {
+        const int ks = t % L::KS, vs = t % L::VS;
+        if (!mbar_wait(&k_full[ks], (t / L::KS) & 1, g)) return false;
+        if (!mbar_wait(&v_full[vs], (t / L::VS) & 1, g)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * L::BOX + (kk & 3) * 32;
+          umma_ss(tmem + L::TM_S, make_sdesc_sw128(q_addr + off, 16, 1024),
+                  make_sdesc_sw128(k_addr + ks * L::TILE + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * L::BOX + (kk & 3) * 32;
+          umma_ss(tmem + L::TM_DS, make_sdesc_sw128(do_addr + off, 16, 1024),
+                  make_sdesc_sw128(v_addr + vs * L::TILE + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&v_empty[vs]);
+        umma_commit(s_full);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, g);
+      if (ok) ok = issue_SdS(0);
+      for (int t = 0; ok && t < T; ++t) {
+        ok = mbar_wait(s_free, t & 1, g);
+        if (ok && t + 1 < T) ok = issue_SdS(t + 1);
+        if (ok) ok = mbar_wait(&dp_full[t & 1], (t >> 1) & 1, g);
+        if (!ok) break;
+        tc_fence_after();
+        const int ks = t % L::KS;
+        const uint32_t pa = tmem + L::TM_DP + (t & 1) * 64;
+#pragma unroll
+        for (int kk = 0; kk < L::BN / 16; ++kk) {
+          const uint64_t kdesc = make_sdesc_sw128(k_addr + ks * L::TILE + kk * 16 * 128, L::BOX, 1024);
+          umma_ts(tmem + L::TM_DQ, pa + kk * 8, kdesc, idQ, (t > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&k_empty[ks]);
+      }
+      if (ok) umma_commit(dq_done);
+      umma_commit(mma_idle);
+      mbar_drain(mma_idle, 0, g.timeout_ns);
+    }
+  } else {
+    const int t_row = threadIdx.x;
+    const int row = m * L::BM + t_row;
+    const bool row_ok = row < p.Sq;
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const float slope = load_slope(p.slopes, p.slopes_dtype, h);
+    const float c_sig = -p.sm_scale * kLog2e;
+    const float c_a = p.sm_scale * kLog2e;
+    const float slope2 = slope * kLog2e;
+    const size_t ri = (size_t)bh * p.Sq + row;
+    const float lse2 = row_ok ? p.lse[ri] * kLog2e : 0.f;
+    float zs = row_ok ? p.rowsig[ri] : 0.f;
+    const float delta = p.delta[(size_t)bh * p.sq_pad + row];
+    const int lim = row_ok ? (p.causal ? min(row + 1, p.Skv) : p.Skv) : 0;
+    const bool rows_partial = (m * L::BM + L::BM > p.Sq);
+    float cacc = 0.f;
+    float2* carry_row = p.carry + (size_t)bh * p.n_kb64 * p.sq_pad + row;
+    bool ok = true;
+    for (int t = 0; t < T; ++t) {
+      const int key0 = t * L::BN;
+      ok = mbar_wait(s_full, t & 1, g);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const bool masked =
+          rows_partial || (key0 + L::BN > p.Skv) || (p.causal && key0 + L::BN - 1 > m * L::BM);
+      const uint32_t dpa = lane_base + L::TM_DP + (t & 1) * 64;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sreg[32], dsreg[32];
+        tmem_ld32(lane_base + L::TM_S + c * 32, sreg);
+        tmem_ld32(lane_base + L::TM_DS + c * 32, dsreg);
+        tmem_ld_wait32(sreg);
+        tmem_ld_fence32(dsreg);
+        if (c == 3) {
+          tc_fence_before();
+          mbar_arrive(s_free);
+        }
+        if ((c & 1) == 0) {
+          const int kb = 2 * t + (c >> 1);
+          if (kb < p.n_kb64) carry_row[(size_t)kb * p.sq_pad] = make_float2(zs, cacc);
+        }
+        uint32_t dpo[16];
+        if (masked)
+          bwd_chunk<true, BF16, false>(sreg, dsreg, key0 + c * 32, lim, c_sig, c_a, slope, slope2, lse2, delta,
+                                       zs, cacc, dpo, nullptr);
+        else
+          bwd_chunk<false, BF16, false>(sreg, dsreg, key0 + c * 32, lim, c_sig, c_a, slope, slope2, lse2,
+                                        delta, zs, cacc, dpo, nullptr);
+        tmem_st16(dpa + c * 16, dpo);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&dp_full[t & 1]);
+    }
+    if (ok) {
+      ok = mbar_wait(dq_done, 0, g);
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (ok) {
+      tc_fence_after();
+      uint8_t* dst_row = static_cast<uint8_t*>(p.dq) + ri * D * 2;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(lane_base + L::TM_DQ + c * 32, r);
+        tmem_ld_wait32(r);
+        if (row_ok) {
+          uint4* dst = reinterpret_cast<uint4*>(dst_row + c * 64);
+#pragma unroll
+          for (int v4 = 0; v4 < 4; ++v4) {
+            uint4 pk;
+            pk.x = pack2<BF16>(__uint_as_float(r[8 * v4 + 0]) * p.sm_scale, __uint_as_float(r[8 * v4 + 1]) * p.sm_scale);
+            pk.y = pack2<BF16>(__uint_as_float(r[8 * v4 + 2]) * p.sm_scale, __uint_as_float(r[8 * v4 + 3]) * p.sm_scale);
+            pk.z = pack2<BF16>(__uint_as_float(r[8 * v4 + 4]) * p.sm_scale, __uint_as_float(r[8 * v4 + 5]) * p.sm_scale);
+            pk.w = pack2<BF16>(__uint_as_float(r[8 * v4 + 6]) * p.sm_scale, __uint_as_float(r[8 * v4 + 7]) * p.sm_scale);
+            dst[v4] = pk;
+          }
+        }
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 3. pass B: dK, dV
+// ---------------------------------------------------------------------------
+template <int D>
+struct BwdBLayout {
+  static constexpr bool TRANS = (D == 128);      // accumulate dV^T / dK^T (M = D)
+  static constexpr int KB = TRANS ? 64 : 128;    // keys per CTA
+  static constexpr int NS = TRANS ? 2 : 1;       // S / dS TMEM buffers
+  static constexpr int QS = 2, PS = 2;           // Q/dO and P/dP shared-memory stages
+  static constexpr int QBOX = 128 * 128;         // [128 rows][64 cols] box
+  static constexpr int KBOX = KB * 128;          // [KB rows][64 cols] box
+  static constexpr int KTILE = KB * D * 2;
+  static constexpr int QB = 128 * D * 2;
+  static constexpr int PB = 128 * KB * 2;        // one P (or dP) tile: [128 rows][KB keys]
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = KTILE;
+  static constexpr int OFF_QDO = 2 * KTILE;      // QS stages of (Q, dO)
+  static constexpr int OFF_P = OFF_QDO + QS * 2 * QB;  // PS stages of (P, dP)
+  static constexpr int OFF_BAR = OFF_P + PS * 2 * PB;
+  static constexpr int NBAR = 1 + 2 * QS + 2 * PS + 2 + 1 + 1 + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int BYTES = OFF_MISC + 16;
+  static constexpr int ALLOC = BYTES + 1024;
+  static constexpr uint32_t TM_S = 0;                 // NS buffers of KB columns
+  static constexpr uint32_t TM_DS = NS * KB;          // NS buffers of KB columns
+  static constexpr uint32_t TM_DV = 2 * NS * KB;      // TRANS: KB columns (lanes = d); else D columns (lanes = keys)
+  static constexpr uint32_t TM_DK = TM_DV + (TRANS ? KB : D);
+  static constexpr uint32_t TM_COLS = 512;
+  static_assert(TM_DK + (TRANS ? KB : D) <= 512, "TMEM budget");
+};
+
+__device__ __forceinline__ void decode_block(int L, int n_heads, int n_blocks, int& hk, int& blk) {
+  // groups of 8 kv heads; within a group the lowest key blocks (most causal work) first
+  const int per_group = 8 * n_blocks;
+  const int grp = L / per_group;
+  const int r = L - grp * per_group;
+  const int g0 = grp * 8;
+  const int gsz = min(8, n_heads - g0);
+  blk = r / gsz;
+  hk = g0 + (r - blk * gsz);
+}
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(192, 1)
+    coalibi_bwd_b_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                         const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                         const BwdParams p) {
+  using L = BwdBLayout<D>;
+  constexpr int KB = L::KB;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem + L::OFF_K;
+  uint8_t* sV = smem + L::OFF_V;
+  uint8_t* sQDO = smem + L::OFF_QDO;
+  uint8_t* sP = smem + L::OFF_P;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* kv_full = bars;
+  uint64_t* qdo_full = kv_full + 1;
+  uint64_t* qdo_empty = qdo_full + L::QS;
+  uint64_t* pp_full = qdo_empty + L::QS;
+  uint64_t* pp_empty = pp_full + L::PS;
+  uint64_t* s_full = pp_empty + L::PS;  // 2
+  uint64_t* s_free = s_full + 2;
+  uint64_t* acc_done = s_free + 1;
+  uint64_t* mma_idle = acc_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  int hk, blk;
+  decode_block(blockIdx.x, p.B * p.Hkv, p.n_blocks, hk, blk);  // hk = b * Hkv + g
+  const int b = hk / p.Hkv;
+  const int gkv = hk - b * p.Hkv;
+  const int G = p.Hq / p.Hkv;
+  const int key0 = blk * KB;
+  const int m_start = p.causal ? key0 / 128 : 0;
+  const int nM = max(0, p.n_qtiles - m_start);
+  const int NIT = G * nM;
+  CtaGuard g{abort_flag, p.status, p.timeout_ns};
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < L::QS; ++i) {
+      mbar_init(&qdo_full[i], 1);
+      mbar_init(&qdo_empty[i], 1);
+    }
+    for (int i = 0; i < L::PS; ++i) {
+      mbar_init(&pp_full[i], 128);
+      mbar_init(&pp_empty[i], 1);
+    }
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
+    mbar_init(s_free, 128);
+    mbar_init(acc_done, 1);
+    mbar_init(mma_idle, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, L::TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0 && NIT > 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmDO);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(kv_full, 2 * L::KTILE);
+#pragma unroll
+      for (int bx = 0; bx < D / 64; ++bx) {
+        tma_load_3d(sK + bx * L::KBOX, &tmK, kv_full, bx * 64, key0, hk);
+        tma_load_3d(sV + bx * L::KBOX, &tmV, kv_full, bx * 64, key0, hk);
+      }
+      int nq = 0;
+      for (int it = 0; it < NIT; ++it) {
+        const int hh = gkv * G + it / nM;
+        const int m = m_start + it % nM;
+        const int bhq = b * p.Hq + hh;
+        const int st = it % L::QS;
+        if (!mbar_wait(&qdo_empty[st], ((it / L::QS) & 1) ^ 1, g)) break;
+        mbar_arrive_expect_tx(&qdo_full[st], 2 * L::QB);
+        uint8_t* sq = sQDO + st * 2 * L::QB;
+#pragma unroll
+        for (int bx = 0; bx < D / 64; ++bx) {
+          tma_load_3d(sq + bx * L::QBOX, &tmQ, &qdo_full[st], bx * 64, m * 128, bhq);
+          tma_load_3d(sq + L::QB + bx * L::QBOX, &tmDO, &qdo_full[st], bx * 64, m * 128, bhq);
+        }
+        ++nq;
+      }
+      mbar_drain(kv_full, 0, g.timeout_ns);
+      for (int s = 0; s < L::QS; ++s) {
+        const int uses = (nq > s) ? (nq - 1 - s) / L::QS + 1 : 0;
+        if (uses > 0) mbar_drain(&qdo_full[s], (uses - 1) & 1, g.timeout_ns);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0 && NIT > 0) {
+      constexpr uint32_t idS = make_idesc_f16(BF16, 128, KB, false, false);
+      // TRANS: dV^T[d][key] = dO^T[d][row] P[row][key]  (A = dO^T MN-major, B = P MN-major), M = D, N = KB
+      // else : dV[key][d]   = P^T[key][row] dO[row][d]  (A = P^T MN-major, B = dO MN-major),  M = KB, N = D
+      constexpr uint32_t idAcc = L::TRANS ? make_idesc_f16(BF16, D, KB, true, true)
+                                          : make_idesc_f16(BF16, KB, D, true, true);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      const uint32_t qdo_addr = smem_u32(sQDO), p_addr = smem_u32(sP);
+      auto issue_SdS = [&](int it) -> bool {
+        const int st = it % L::QS;
+        if (!mbar_wait(&qdo_full[st], (it / L::QS) & 1, g)) return false;
+        tc_fence_after();
+        const uint32_t qa = qdo_addr + st * 2 * L::QB, da = qa + L::QB;
+        const int sb = it % L::NS;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t qo = (kk >> 2) * L::QBOX + (kk & 3) * 32;
+          const uint32_t ko = (kk >> 2) * L::KBOX + (kk & 3) * 32;
+          umma_ss(tmem + L::TM_S + sb * KB, make_sdesc_sw128(qa + qo, 16, 1024),
+                  make_sdesc_sw128(k_addr + ko, 16, 1024), idS, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t qo = (kk >> 2) * L::QBOX + (kk & 3) * 32;
+          const uint32_t ko = (kk >> 2) * L::KBOX + (kk & 3) * 32;
+          umma_ss(tmem + L::TM_DS + sb * KB, make_sdesc_sw128(da + qo, 16, 1024),
+                  make_sdesc_sw128(v_addr + ko, 16, 1024), idS, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[sb]);
+        return true;
+      };
+      bool ok = mbar_wait(kv_full, 0, g);
+      if (ok) ok = issue_SdS(0);
+      for (int it = 0; ok && it < NIT; ++it) {
+        if (it + 1 < NIT) {
+          if (L::NS == 1) ok = mbar_wait(s_free, it & 1, g);
+          if (ok) ok = issue_SdS(it + 1);
+        }
+        const int ps = it % L::PS;
+        if (ok) ok = mbar_wait(&pp_full[ps], (it / L::PS) & 1, g);
+        if (!ok) break;
+        tc_fence_after();
+        const int st = it % L::QS;
+        const uint32_t qa = qdo_addr + st * 2 * L::QB, da = qa + L::QB;
+        const uint32_t pa = p_addr + ps * 2 * L::PB, dpa = pa + L::PB;
+        const uint32_t acc = (it > 0) ? 1u : 0u;
+#pragma unroll
+        for (int kk = 0; kk < 128 / 16; ++kk) {  // K = 128 query rows, 16 per MMA
+          const uint32_t ko = kk * 16 * 128;        // 16 rows of 128 bytes
+          if (L::TRANS) {
+            // A: dO^T / Q^T (MN = d, 64-wide blocks one box apart), B: P / dP (MN = keys, one block)
+            umma_ss(tmem + L::TM_DV, make_sdesc_sw128(da + ko, L::QBOX, 1024),
+                    make_sdesc_sw128(pa + ko, L::PB, 1024), idAcc, (acc || kk > 0) ? 1u : 0u);
+            umma_ss(tmem + L::TM_DK, make_sdesc_sw128(qa + ko, L::QBOX, 1024),
+                    make_sdesc_sw128(dpa + ko, L::PB, 1024), idAcc, (acc || kk > 0) ? 1u : 0u);
+          } else {
+            // A: P^T / dP^T (MN = keys, two 64-key blocks 128*128 bytes apart), B: dO / Q (MN = d)
+            umma_ss(tmem + L::TM_DV, make_sdesc_sw128(pa + ko, 128 * 128, 1024),
+                    make_sdesc_sw128(da + ko, L::QBOX, 1024), idAcc, (acc || kk > 0) ? 1u : 0u);
+            umma_ss(tmem + L::TM_DK, make_sdesc_sw128(dpa + ko, 128 * 128, 1024),
+                    make_sdesc_sw128(qa + ko, L::QBOX, 1024), idAcc, (acc || kk > 0) ? 1u : 0u);
+          }
+        }
+        umma_commit(&pp_empty[ps]);
+        umma_commit(&qdo_empty[st]);
+      }
+      if (ok) umma_commit(acc_done);
+      umma_commit(mma_idle);
+      mbar_drain(mma_idle, 0, g.timeout_ns);
+    }
+  } else {
+    const int t_row = threadIdx.x;
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const float c_sig = -p.sm_scale * kLog2e;
+    const float c_a = p.sm_scale * kLog2e;
+    const int kb64 = key0 / 64;
+    bool ok = true;
+    for (int it = 0; it < NIT; ++it) {
+      const int hh = gkv * G + it / nM;
+      const int m = m_start + it % nM;
+      const int bhq = b * p.Hq + hh;
+      const int row = m * 128 + t_row;
+      const bool row_ok = row < p.Sq;
+      const float slope = load_slope(p.slopes, p.slopes_dtype, hh);
+      const float slope2 = slope * kLog2e;
+      const size_t ri = (size_t)bhq * p.Sq + row;
+      const float lse2 = row_ok ? p.lse[ri] * kLog2e : 0.f;
+      const float delta = p.delta[(size_t)bhq * p.sq_pad + row];
+      const float2 cin = p.carry[((size_t)bhq * p.n_kb64 + kb64) * p.sq_pad + row];
+      float zs = cin.x, cacc = cin.y;
+      const int lim = row_ok ? (p.causal ? min(row + 1, p.Skv) : p.Skv) : 0;
+      const bool masked = (m * 128 + 128 > p.Sq) || (key0 + KB > p.Skv) || (p.causal && key0 + KB - 1 > m * 128);
+
+      const int sb = it % L::NS;
+      ok = mbar_wait(&s_full[sb], (it / L::NS) & 1, g);
+      const int ps = it % L::PS;
+      if (ok) ok = mbar_wait(&pp_empty[ps], ((it / L::PS) & 1) ^ 1, g);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      uint8_t* prow = sP + ps * 2 * L::PB;
+      uint8_t* dprow = prow + L::PB;
+      const uint32_t rsw = t_row & 7;
+      const uint32_t rbase = (t_row >> 3) * 1024 + rsw * 128;
+#pragma unroll 1
+      for (int c = 0; c < KB / 32; ++c) {
+        uint32_t sreg[32], dsreg[32];
+        tmem_ld32(lane_base + L::TM_S + sb * KB + c * 32, sreg);
+        tmem_ld32(lane_base + L::TM_DS + sb * KB + c * 32, dsreg);
+        tmem_ld_wait32(sreg);
+        tmem_ld_fence32(dsreg);
+        if (L::NS == 1 && c == KB / 32 - 1) {
+          tc_fence_before();
+          mbar_arrive(s_free);
+        }
+        uint32_t po[16], dpo[16];
+        if (masked)
+          bwd_chunk<true, BF16, true>(sreg, dsreg, key0 + c * 32, lim, c_sig, c_a, slope, slope2, lse2, delta, zs,
+                                      cacc, dpo, po);
+        else
+          bwd_chunk<false, BF16, true>(sreg, dsreg, key0 + c * 32, lim, c_sig, c_a, slope, slope2, lse2, delta,
+                                       zs, cacc, dpo, po);
+        // 32 keys = four 16-byte chunks; 64-key swizzle rows, 128x128-byte blocks
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int chunk = c * 4 + u;          // 8-key chunk index within the KB keys
+          const uint32_t blk64 = chunk >> 3;    // which 64-key block
+          const uint32_t cc = chunk & 7;
+          const uint32_t off = blk64 * (128 * 128) + rbase + ((cc ^ rsw) << 4);
+          *reinterpret_cast<uint4*>(prow + off) = make_uint4(po[4 * u], po[4 * u + 1], po[4 * u + 2], po[4 * u + 3]);
+          *reinterpret_cast<uint4*>(dprow + off) =
+              make_uint4(dpo[4 * u], dpo[4 * u + 1], dpo[4 * u + 2], dpo[4 * u + 3]);
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(&pp_full[ps]);
+    }
+    // epilogue
+    const int bkv = hk;
+    if (NIT > 0) {
+      if (ok) {
+        ok = mbar_wait(acc_done, 0, g);
+        ok = __all_sync(0xffffffffu, ok);
+      }
+      if (ok) {
+        tc_fence_after();
+        if (L::TRANS) {
+          // lane t = d; columns = keys of this block
+          const int d = t_row;
+#pragma unroll 1
+          for (int c = 0; c < KB / 32; ++c) {
+            uint32_t rv[32], rk[32];
+            tmem_ld32(lane_base + L::TM_DV + c * 32, rv);
+            tmem_ld32(lane_base + L::TM_DK + c * 32, rk);
+            tmem_ld_wait32(rv);
+            tmem_ld_fence32(rk);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int key = key0 + c * 32 + j;
+              if (key < p.Skv) {
+                const size_t o = ((size_t)bkv * p.Skv + key) * D + d;
+                const uint32_t pv = pack2<BF16>(__uint_as_float(rv[j]), 0.f);
+                const uint32_t pk = pack2<BF16>(__uint_as_float(rk[j]) * p.sm_scale, 0.f);
+                static_cast<uint16_t*>(p.dv)[o] = (uint16_t)(pv & 0xffffu);
+                static_cast<uint16_t*>(p.dk)[o] = (uint16_t)(pk & 0xffffu);
+              }
+            }
+          }
+        } else {
+          // lane t = key; columns = d
+          const int key = key0 + t_row;
+          uint8_t* dvrow = static_cast<uint8_t*>(p.dv) + ((size_t)bkv * p.Skv + key) * D * 2;
+          uint8_t* dkrow = static_cast<uint8_t*>(p.dk) + ((size_t)bkv * p.Skv + key) * D * 2;
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t rv[32], rk[32];
+            tmem_ld32(lane_base + L::TM_DV + c * 32, rv);
+            tmem_ld32(lane_base + L::TM_DK + c * 32, rk);
+            tmem_ld_wait32(rv);
+            tmem_ld_fence32(rk);
+            if (key < p.Skv) {
+#pragma unroll
+              for (int v4 = 0; v4 < 4; ++v4) {
+                uint4 a, bb;
+                a.x = pack2<BF16>(__uint_as_float(rv[8 * v4 + 0]), __uint_as_float(rv[8 * v4 + 1]));
+                a.y = pack2<BF16>(__uint_as_float(rv[8 * v4 + 2]), __uint_as_float(rv[8 * v4 + 3]));
+                a.z = pack2<BF16>(__uint_as_float(rv[8 * v4 + 4]), __uint_as_float(rv[8 * v4 + 5]));
+                a.w = pack2<BF16>(__uint_as_float(rv[8 * v4 + 6]), __uint_as_float(rv[8 * v4 + 7]));
+                const float s = p.sm_scale;
+                bb.x = pack2<BF16>(__uint_as_float(rk[8 * v4 + 0]) * s, __uint_as_float(rk[8 * v4 + 1]) * s);
+                bb.y = pack2<BF16>(__uint_as_float(rk[8 * v4 + 2]) * s, __uint_as_float(rk[8 * v4 + 3]) * s);
+                bb.z = pack2<BF16>(__uint_as_float(rk[8 * v4 + 4]) * s, __uint_as_float(rk[8 * v4 + 5]) * s);
+                bb.w = pack2<BF16>(__uint_as_float(rk[8 * v4 + 6]) * s, __uint_as_float(rk[8 * v4 + 7]) * s);
+                reinterpret_cast<uint4*>(dvrow + c * 64)[v4] = a;
+                reinterpret_cast<uint4*>(dkrow + c * 64)[v4] = bb;
+              }
+            }
+          }
+        }
+      }
+    } else {
+      // no query row sees these keys: their gradients are zero
+      if (L::TRANS) {
+        const int d = t_row;
+        for (int j = 0; j < KB; ++j) {
+          const int key = key0 + j;
+          if (key < p.Skv) {
+            const size_t o = ((size_t)bkv * p.Skv + key) * D + d;
+            static_cast<uint16_t*>(p.dv)[o] = 0;
+            static_cast<uint16_t*>(p.dk)[o] = 0;
+          }
+        }
+      } else {
+        const int key = key0 + t_row;
+        if (key < p.Skv) {
+          uint4* dvrow = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.dv) + ((size_t)bkv * p.Skv + key) * D * 2);
+          uint4* dkrow = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.dk) + ((size_t)bkv * p.Skv + key) * D * 2);
+          for (int v4 = 0; v4 < D / 8; ++v4) {
+            dvrow[v4] = make_uint4(0, 0, 0, 0);
+            dkrow[v4] = make_uint4(0, 0, 0, 0);
+          }
+        }
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host-side helpers (called from coalibi.cu)
+// ---------------------------------------------------------------------------
+int make_tmap(CUtensorMap* map, const void* base, int D, int rows, int heads, int box_rows, bool bf16);
+
+template <typename K>
+inline bool bwd_set_smem_one(K kernel, int bytes) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess;
+}
+
+inline bool bwd_set_smem_attributes() {
+  bool ok = true;
+  ok &= bwd_set_smem_one(coalibi_bwd_a_kernel<128, false>, BwdALayout<128>::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_a_kernel<128, true>, BwdALayout<128>::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_a_kernel<64, false>, BwdALayout<64>::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_a_kernel<64, true>, BwdALayout<64>::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_b_kernel<128, false>, BwdBLayout<128>::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_b_kernel<128, true>, BwdBLayout<128>::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_b_kernel<64, false>, BwdBLayout<64>::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_b_kernel<64, true>, BwdBLayout<64>::ALLOC);
+  return ok;
+}
+
+template <int D, bool BF16>
+inline int bwd_launch_t(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigned long long tmo,
+                        cudaStream_t stream, int phases) {
+  BwdParams p{};
+  p.o = a.o;
+  p.dout = a.dout;
+  p.lse = a.lse;
+  p.rowsig = a.rowsig;
+  p.slopes = a.slopes;
+  p.dq = a.dq;
+  p.dk = a.dk;
+  p.dv = a.dv;
+  p.delta = reinterpret_cast<float*>(static_cast<uint8_t*>(a.workspace) + ws.delta_off);
+  p.carry = reinterpret_cast<float2*>(static_cast<uint8_t*>(a.workspace) + ws.carry_off);
+  p.B = a.B;
+  p.Hq = a.Hq;
+  p.Hkv = a.Hkv;
+  p.Sq = a.Sq;
+  p.Skv = a.Skv;
+  p.slopes_dtype = a.slopes_dtype;
+  p.causal = a.causal ? 1 : 0;
+  p.sm_scale = a.sm_scale;
+  p.status = a.status;
+  p.timeout_ns = tmo;
+  p.n_qtiles = (a.Sq + 127) / 128;
+  p.n_kvtiles = (a.Skv + 127) / 128;
+  p.n_kb64 = (a.Skv + 63) / 64;
+  p.n_blocks = (a.Skv + BwdBLayout<D>::KB - 1) / BwdBLayout<D>::KB;
+  p.sq_pad = p.n_qtiles * 128;
+
+  CUtensorMap tq, tdo, tk, tv, tkb, tvb;
+  int rc;
+  if ((rc = make_tmap(&tq, a.q, D, a.Sq, a.B * a.Hq, 128, BF16))) return rc;
+  if ((rc = make_tmap(&tdo, a.dout, D, a.Sq, a.B * a.Hq, 128, BF16))) return rc;
+  if ((rc = make_tmap(&tk, a.k, D, a.Skv, a.B * a.Hkv, 128, BF16))) return rc;
+  if ((rc = make_tmap(&tv, a.v, D, a.Skv, a.B * a.Hkv, 128, BF16))) return rc;
+  if ((rc = make_tmap(&tkb, a.k, D, a.Skv, a.B * a.Hkv, BwdBLayout<D>::KB, BF16))) return rc;
+  if ((rc = make_tmap(&tvb, a.v, D, a.Skv, a.B * a.Hkv, BwdBLayout<D>::KB, BF16))) return rc;
+
+  const long long rows = (long long)a.B * a.Hq * p.sq_pad;
+  if (phases & 1)
+    coalibi_bwd_delta_kernel<D, BF16><<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(p);
+  if (phases & 2)
+    coalibi_bwd_a_kernel<D, BF16><<<a.B * a.Hq * p.n_qtiles, 192, BwdALayout<D>::ALLOC, stream>>>(tq, tdo, tk, tv, p);
+  if (phases & 4)
+    coalibi_bwd_b_kernel<D, BF16><<<a.B * a.Hkv * p.n_blocks, 192, BwdBLayout<D>::ALLOC, stream>>>(tq, tdo, tkb, tvb, p);
+  return cudaGetLastError() == cudaSuccess ? COALIBI_OK : COALIBI_ERR_LAUNCH;
+}
+
+inline int bwd_launch(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigned long long tmo,
+                      cudaStream_t stream, int phases) {
+  const bool bf16 = a.dtype == COALIBI_BF16;
+  if (a.D == 128)
+    return bf16 ? bwd_launch_t<128, true>(a, ws, tmo, stream, phases)
+                : bwd_launch_t<128, false>(a, ws, tmo, stream, phases);
+  return bf16 ? bwd_launch_t<64, true>(a, ws, tmo, stream, phases)
+              : bwd_launch_t<64, false>(a, ws, tmo, stream, phases);
+}
+
+}  // namespace coalibi

@@ -1,0 +1,247 @@
+// C-ABI entry points of libcoalibi_sm100.so (declared in include/coalibi.h):
+// argument validation, TMA tensor-map encoding and kernel dispatch.  Nothing
+// here allocates device memory or synchronises.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "coalibi.h"
+#include "fwd.cuh"
+#include "bwd.cuh"
+
+namespace coalibi {
+
+// Human-readable detail of the last failure on this thread (coalibi_last_error()).
+static thread_local char g_last_error[256] = "";
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 3-D view (D, rows, heads) of a contiguous [.., heads, rows, D] 16-bit tensor,
+// loaded as boxes of 64 columns x box_rows rows with the 128-byte swizzle the
+// UMMA descriptors expect.  Rows past `rows` read as zero.
+int make_tmap(CUtensorMap* map, const void* base, int D, int rows, int heads, int box_rows, bool bf16) {
+  auto fn = encode_fn();
+  if (fn == nullptr) {
+    snprintf(g_last_error, sizeof(g_last_error), "cuTensorMapEncodeTiled unavailable from the driver");
+    return COALIBI_ERR_TENSOR_MAP;
+  }
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)rows, (cuuint64_t)heads};
+  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)rows * D * 2};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    snprintf(g_last_error, sizeof(g_last_error),
+             "cuTensorMapEncodeTiled -> %d (base=%p D=%d rows=%d heads=%d box_rows=%d map=%p)", (int)r, base, D,
+             rows, heads, box_rows, (void*)map);
+    return COALIBI_ERR_TENSOR_MAP;
+  }
+  return COALIBI_OK;
+}
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr unsigned kDefaultTimeoutMs = 2000;
+
+// Per-device one-time setup: architecture check and opt-in shared memory sizes.
+struct DeviceState {
+  std::once_flag once;
+  int status = COALIBI_ERR_DEVICE;
+};
+DeviceState g_dev[kMaxDevices];
+
+template <typename K>
+bool set_smem(K kernel, int bytes) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess;
+}
+
+// Make the device that owns `ptr` current on the calling thread and bind its
+// primary context.  Callers such as autograd's backward worker threads may
+// reach us with no context current, which the tensor-map encoder rejects.
+int bind_device(const void* ptr) {
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, ptr) != cudaSuccess) {
+    cudaGetLastError();
+    snprintf(g_last_error, sizeof(g_last_error), "cudaPointerGetAttributes failed for %p", ptr);
+    return COALIBI_ERR_DEVICE;
+  }
+  if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged) {
+    snprintf(g_last_error, sizeof(g_last_error), "%p is not a device pointer", ptr);
+    return COALIBI_ERR_DEVICE;
+  }
+  if (cudaSetDevice(attr.device) != cudaSuccess) {
+    cudaGetLastError();
+    snprintf(g_last_error, sizeof(g_last_error), "cudaSetDevice(%d) failed", attr.device);
+    return COALIBI_ERR_DEVICE;
+  }
+  return COALIBI_OK;
+}
+
+int device_setup(const void* ptr) {
+  if (int rc = bind_device(ptr)) return rc;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return COALIBI_ERR_DEVICE;
+  DeviceState& st = g_dev[dev];
+  std::call_once(st.once, [&st, dev] {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (major != 10 || minor != 0) {
+      st.status = COALIBI_ERR_DEVICE;
+      return;
+    }
+    bool ok = true;
+    ok &= set_smem(coalibi_fwd_kernel<128, false>, FwdLayout<128>::ALLOC);
+    ok &= set_smem(coalibi_fwd_kernel<128, true>, FwdLayout<128>::ALLOC);
+    ok &= set_smem(coalibi_fwd_kernel<64, false>, FwdLayout<64>::ALLOC);
+    ok &= set_smem(coalibi_fwd_kernel<64, true>, FwdLayout<64>::ALLOC);
+    ok &= bwd_set_smem_attributes();
+    st.status = ok ? COALIBI_OK : COALIBI_ERR_LAUNCH;
+  });
+  return st.status;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_common(int B, int Hq, int Hkv, int Sq, int Skv, int D, int dtype, int slopes_dtype) {
+  if (D != 64 && D != 128) return COALIBI_ERR_HEAD_DIM;
+  if (dtype != COALIBI_F16 && dtype != COALIBI_BF16) return COALIBI_ERR_DTYPE;
+  if (slopes_dtype != COALIBI_F16 && slopes_dtype != COALIBI_BF16 && slopes_dtype != COALIBI_F32)
+    return COALIBI_ERR_DTYPE;
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || Skv <= 0) return COALIBI_ERR_SHAPE;
+  if (Hq % Hkv != 0) return COALIBI_ERR_SHAPE;
+  const long long nq = (Sq + 127) / 128;
+  if ((long long)B * Hq * nq > 0x7fffffffLL) return COALIBI_ERR_SHAPE;
+  if ((long long)B * Hq > 0x7fffffffLL || (long long)B * Hkv * Skv > (1LL << 40)) return COALIBI_ERR_SHAPE;
+  return COALIBI_OK;
+}
+
+unsigned long long timeout_ns(unsigned ms) {
+  return (unsigned long long)(ms == 0 ? kDefaultTimeoutMs : ms) * 1000000ull;
+}
+
+template <int D, bool BF16>
+int launch_fwd_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const FwdParams& p,
+               cudaStream_t stream) {
+  const int grid = p.B * p.Hq * p.n_qtiles;
+  coalibi_fwd_kernel<D, BF16><<<grid, 192, FwdLayout<D>::ALLOC, stream>>>(tq, tk, tv, p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    snprintf(g_last_error, sizeof(g_last_error), "forward launch: %s", cudaGetErrorString(e));
+    return COALIBI_ERR_LAUNCH;
+  }
+  return COALIBI_OK;
+}
+
+template <int D, bool BF16>
+int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const FwdParams& p,
+               cudaStream_t stream) {
+  return launch_fwd_impl<D, BF16>(tq, tk, tv, p, stream);
+}
+
+}  // namespace
+}  // namespace coalibi
+
+using namespace coalibi;
+
+extern "C" int coalibi_fwd(const CoalibiFwdArgs* a, void* stream) {
+  if (a == nullptr) return COALIBI_ERR_NULL_POINTER;
+  if (!a->q || !a->k || !a->v || !a->o || !a->lse || !a->rowsig || !a->slopes) return COALIBI_ERR_NULL_POINTER;
+  int rc = check_common(a->B, a->Hq, a->Hkv, a->Sq, a->Skv, a->D, a->dtype, a->slopes_dtype);
+  if (rc) return rc;
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o)) return COALIBI_ERR_ALIGNMENT;
+  if ((rc = device_setup(a->q))) return rc;
+  const bool bf16 = a->dtype == COALIBI_BF16;
+  CUtensorMap tq, tk, tv;
+  if ((rc = make_tmap(&tq, a->q, a->D, a->Sq, a->B * a->Hq, 128, bf16))) return rc;
+  if ((rc = make_tmap(&tk, a->k, a->D, a->Skv, a->B * a->Hkv, 128, bf16))) return rc;
+  if ((rc = make_tmap(&tv, a->v, a->D, a->Skv, a->B * a->Hkv, 128, bf16))) return rc;
+  FwdParams p{};
+  p.o = a->o;
+  p.lse = a->lse;
+  p.rowsig = a->rowsig;
+  p.slopes = a->slopes;
+  p.B = a->B;
+  p.Hq = a->Hq;
+  p.Hkv = a->Hkv;
+  p.Sq = a->Sq;
+  p.Skv = a->Skv;
+  p.slopes_dtype = a->slopes_dtype;
+  p.causal = a->causal ? 1 : 0;
+  p.sm_scale = a->sm_scale;
+  p.status = a->status;
+  p.timeout_ns = timeout_ns(a->timeout_ms);
+  p.n_qtiles = (a->Sq + 127) / 128;
+  p.n_kvtiles = (a->Skv + 127) / 128;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (a->D == 128) return bf16 ? launch_fwd<128, true>(tq, tk, tv, p, s) : launch_fwd<128, false>(tq, tk, tv, p, s);
+  return bf16 ? launch_fwd<64, true>(tq, tk, tv, p, s) : launch_fwd<64, false>(tq, tk, tv, p, s);
+}
+
+extern "C" size_t coalibi_bwd_workspace_bytes(int B, int Hq, int Hkv, int Sq, int Skv, int D) {
+  (void)Hkv;
+  (void)D;
+  if (B <= 0 || Hq <= 0 || Sq <= 0 || Skv <= 0) return 0;
+  return bwd_workspace_layout(B, Hq, Sq, Skv).total;
+}
+
+extern "C" int coalibi_bwd_phases(const CoalibiBwdArgs* a, int phase_mask, void* stream) {
+  if (a == nullptr) return COALIBI_ERR_NULL_POINTER;
+  if (phase_mask & ~7) return COALIBI_ERR_SHAPE;
+  if (!a->q || !a->k || !a->v || !a->o || !a->dout || !a->lse || !a->rowsig || !a->slopes || !a->dq || !a->dk ||
+      !a->dv)
+    return COALIBI_ERR_NULL_POINTER;
+  int rc = check_common(a->B, a->Hq, a->Hkv, a->Sq, a->Skv, a->D, a->dtype, a->slopes_dtype);
+  if (rc) return rc;
+  const void* ptrs[8] = {a->q, a->k, a->v, a->o, a->dout, a->dq, a->dk, a->dv};
+  for (const void* ptr : ptrs)
+    if (!aligned16(ptr)) return COALIBI_ERR_ALIGNMENT;
+  const BwdWorkspace ws = bwd_workspace_layout(a->B, a->Hq, a->Sq, a->Skv);
+  if (a->workspace == nullptr || a->workspace_bytes < ws.total) return COALIBI_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0) return COALIBI_ERR_ALIGNMENT;
+  if ((rc = device_setup(a->q))) return rc;
+  return bwd_launch(*a, ws, timeout_ns(a->timeout_ms), static_cast<cudaStream_t>(stream), phase_mask);
+}
+
+extern "C" int coalibi_bwd(const CoalibiBwdArgs* a, void* stream) { return coalibi_bwd_phases(a, 7, stream); }
+
+extern "C" const char* coalibi_strerror(int code) {
+  switch (code) {
+    case COALIBI_OK: return "ok";
+    case COALIBI_ERR_NULL_POINTER: return "null pointer argument";
+    case COALIBI_ERR_HEAD_DIM: return "unsupported head dim (expected 64 or 128)";
+    case COALIBI_ERR_DTYPE: return "unsupported dtype (expected float16 or bfloat16)";
+    case COALIBI_ERR_SHAPE: return "invalid shape (non-positive size, Hq % Hkv != 0, or too large)";
+    case COALIBI_ERR_ALIGNMENT: return "pointer not 16-byte aligned (workspace: 256-byte)";
+    case COALIBI_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case COALIBI_ERR_TENSOR_MAP: return "TMA tensor map encoding failed";
+    case COALIBI_ERR_WORKSPACE: return "backward workspace missing or too small";
+    case COALIBI_ERR_DEVICE: return "current CUDA device is not an sm_100 (B200) GPU";
+    case COALIBI_ERR_TIMEOUT: return "a bounded in-kernel wait timed out";
+    default: return "unknown error";
+  }
+}
+
+extern "C" int coalibi_abi_version(void) { return COALIBI_ABI_VERSION; }
+
+extern "C" const char* coalibi_last_error(void) { return g_last_error; }

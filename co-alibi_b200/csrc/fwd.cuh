@@ -1,0 +1,391 @@
+// Co-ALiBi attention forward for sm_100a.
+//
+// One CTA owns a 128-row query tile of one (batch, head) and sweeps the key
+// tiles from RIGHT to LEFT, so the inclusive suffix sum z_ij = sum_{t>=j} s_it
+// of the sigmoids is carried online from tile to tile (the reference kernel
+// co_alibi_attn/co_alibi_fwd_kernel.py:66-113 uses the same sweep direction).
+//
+// Roles (192 threads):
+//   warps 0-3  softmax: thread t owns query row t of the tile.  A tcgen05
+//              32x32b TMEM load hands it the whole score row, so the reverse
+//              suffix scan, the row max and the row sum are sequential
+//              in-register work with no shuffles.
+//   warp  4    TMA producer: Q once, then K and V tiles into separate rings.
+//   warp  5    TMEM allocator + single-thread tcgen05.mma issuer.
+//
+// TMEM (512 columns x 128 lanes, fp32):
+//   [0,128) S buffer 0 | [128,256) S buffer 1 | [256,256+D) O accumulator |
+//   two 64-column P buffers (fp16/bf16 pairs) used as the TMEM A operand of O += P V.
+//
+// Per KV tile n (processing order), the MMA warp issues S_n = Q K_n^T into S
+// buffer n%2 as soon as K_n lands, and O += P_n V_n once the softmax warps
+// publish P_n.  Softmax works in the log2 domain with a lazily updated
+// reference max (O is rescaled in TMEM only when the row max grows by more
+// than 2^8), which is exact because O and l share the same stale reference.
+#pragma once
+
+#include <cuda.h>
+#include "sm100.cuh"
+
+namespace coalibi {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct FwdParams {
+  void* o;
+  float* lse;
+  float* rowsig;
+  const void* slopes;
+  int B, Hq, Hkv, Sq, Skv;
+  int slopes_dtype;
+  int causal;
+  float sm_scale;
+  int* status;
+  unsigned long long timeout_ns;
+  int n_qtiles;
+  int n_kvtiles;
+};
+
+__device__ __forceinline__ float load_slope(const void* slopes, int dtype, int h) {
+  if (dtype == 2) return static_cast<const float*>(slopes)[h];
+  if (dtype == 1) return __bfloat162float(static_cast<const __nv_bfloat16*>(slopes)[h]);
+  return __half2float(static_cast<const __half*>(slopes)[h]);
+}
+
+// Map a linear CTA index to (bh, q_tile): heads are taken in groups of 8 (so the
+// K/V of concurrently running CTAs stay L2 resident) and, within a group, the
+// longest causal rows (highest q tile) go first.
+__device__ __forceinline__ void decode_tile(int L, int BH, int nQ, int& bh, int& m) {
+  const int per_group = 8 * nQ;
+  const int grp = L / per_group;
+  const int r = L - grp * per_group;
+  const int g0 = grp * 8;
+  const int gsz = min(8, BH - g0);
+  const int mq = r / gsz;
+  bh = g0 + (r - mq * gsz);
+  m = nQ - 1 - mq;
+}
+
+template <int D>
+struct FwdLayout {
+  static constexpr int BM = 128, BN = 128;
+  static constexpr int KS = (D == 128) ? 3 : 4;
+  static constexpr int VS = (D == 128) ? 2 : 3;
+  static constexpr int BOX = 128 * 128;  // one [128 rows][64 cols] 16-bit box, SW128
+  static constexpr int TILE = BN * D * 2;
+  static constexpr int QB = BM * D * 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + QB;
+  static constexpr int OFF_V = OFF_K + KS * TILE;
+  static constexpr int OFF_BAR = OFF_V + VS * TILE;
+  static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 2 + 2 + 1 + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int BYTES = OFF_MISC + 16;
+  static constexpr int ALLOC = BYTES + 1024;
+  static constexpr uint32_t TM_S = 0;
+  static constexpr uint32_t TM_O = 256;
+  static constexpr uint32_t TM_P = 256 + D;
+  static constexpr uint32_t TM_COLS = 512;
+};
+
+// Reverse scan of one 128-key score row (raw q.k dot products in sreg[]):
+// sigmoid, suffix sum carried in `run`, penalised log2-domain logit written
+// back into sreg[].  Returns the row max over the tile.  Keys >= lim are masked.
+template <bool MASK>
+__device__ __forceinline__ float fwd_scan_tile(uint32_t* sreg, float& run, int key0, int lim, float c_sig,
+                                               float c_a, float slope2) {
+  float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+  for (int j = 127; j >= 0; --j) {
+    const float x = __uint_as_float(sreg[j]);
+    float sg = sigmoid_from_neg_log2(x * c_sig);
+    if (MASK && key0 + j >= lim) sg = 0.f;
+    run += sg;
+    float a = fmaf(-slope2, run, x * c_a);
+    if (MASK && key0 + j >= lim) a = -INFINITY;
+    sreg[j] = __float_as_uint(a);
+    if ((j & 3) == 0) mx0 = fmaxf(mx0, a);
+    if ((j & 3) == 1) mx1 = fmaxf(mx1, a);
+    if ((j & 3) == 2) mx2 = fmaxf(mx2, a);
+    if ((j & 3) == 3) mx3 = fmaxf(mx3, a);
+  }
+  return fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+}
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(192, 1)
+    coalibi_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
+  using L = FwdLayout<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  uint8_t* sQ = smem + L::OFF_Q;
+  uint8_t* sK = smem + L::OFF_K;
+  uint8_t* sV = smem + L::OFF_V;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + L::KS;
+  uint64_t* v_full = k_empty + L::KS;
+  uint64_t* v_empty = v_full + L::VS;
+  uint64_t* s_full = v_empty + L::VS;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* pv_done = p_full + 2;
+  uint64_t* mma_idle = pv_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int BH = p.B * p.Hq;
+  int bh, m;
+  decode_tile(blockIdx.x, BH, p.n_qtiles, bh, m);
+  const int b = bh / p.Hq;
+  const int h = bh - b * p.Hq;
+  const int kvh = h / (p.Hq / p.Hkv);
+  const int zkv = b * p.Hkv + kvh;
+  // visited key tiles: 0..last (causal: tiles starting at or before the tile's last row)
+  const int last = p.causal ? min(p.n_kvtiles - 1, (m * L::BM + L::BM - 1) / L::BN) : p.n_kvtiles - 1;
+  const int N = last + 1;
+
+  CtaGuard g{abort_flag, p.status, p.timeout_ns};
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < L::KS; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < L::VS; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+    }
+    mbar_init(pv_done, 1);
+    mbar_init(mma_idle, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, L::TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(q_full, L::QB);
+#pragma unroll
+      for (int bx = 0; bx < D / 64; ++bx) tma_load_3d(sQ + bx * L::BOX, &tmQ, q_full, bx * 64, m * L::BM, bh);
+      int nk = 0, nv = 0;
+      for (int n = 0; n < N; ++n) {
+        const int key0 = (last - n) * L::BN;
+        const int ks = n % L::KS;
+        if (!mbar_wait(&k_empty[ks], ((n / L::KS) & 1) ^ 1, g)) break;
+        mbar_arrive_expect_tx(&k_full[ks], L::TILE);
+#pragma unroll
+        for (int bx = 0; bx < D / 64; ++bx)
+          tma_load_3d(sK + ks * L::TILE + bx * L::BOX, &tmK, &k_full[ks], bx * 64, key0, zkv);
+        ++nk;
+        const int vs = n % L::VS;
+        if (!mbar_wait(&v_empty[vs], ((n / L::VS) & 1) ^ 1, g)) break;
+        mbar_arrive_expect_tx(&v_full[vs], L::TILE);
+#pragma unroll
+        for (int bx = 0; bx < D / 64; ++bx)
+          tma_load_3d(sV + vs * L::TILE + bx * L::BOX, &tmV, &v_full[vs], bx * 64, key0, zkv);
+        ++nv;
+      }
+      // Drain: every issued copy must have landed before the CTA may exit.
+      mbar_drain(q_full, 0, g.timeout_ns);
+      for (int s = 0; s < L::KS; ++s) {
+        const int uses = (nk > s) ? (nk - 1 - s) / L::KS + 1 : 0;
+        if (uses > 0) mbar_drain(&k_full[s], (uses - 1) & 1, g.timeout_ns);
+      }
+      for (int s = 0; s < L::VS; ++s) {
+        const int uses = (nv > s) ? (nv - 1 - s) / L::VS + 1 : 0;
+        if (uses > 0) mbar_drain(&v_full[s], (uses - 1) & 1, g.timeout_ns);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idS = make_idesc_f16(BF16, 128, L::BN, false, false);
+      constexpr uint32_t idPV = make_idesc_f16(BF16, 128, D, false, true);
+      const uint32_t q_addr = smem_u32(sQ);
+      const uint32_t k_addr = smem_u32(sK);
+      const uint32_t v_addr = smem_u32(sV);
+      auto issue_S = [&](int n) -> bool {
+        const int ks = n % L::KS;
+        if (!mbar_wait(&k_full[ks], (n / L::KS) & 1, g)) return false;
+        tc_fence_after();
+        const uint32_t d = tmem + L::TM_S + (n & 1) * 128;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * L::BOX + (kk & 3) * 32;
+          umma_ss(d, make_sdesc_sw128(q_addr + off, 16, 1024),
+                  make_sdesc_sw128(k_addr + ks * L::TILE + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&k_empty[ks]);
+        umma_commit(&s_full[n & 1]);
+        return true;
+      };
+      auto issue_PV = [&](int n) -> bool {
+        if (!mbar_wait(&p_full[n & 1], (n >> 1) & 1, g)) return false;
+        const int vs = n % L::VS;
+        if (!mbar_wait(&v_full[vs], (n / L::VS) & 1, g)) return false;
+        tc_fence_after();
+        const uint32_t pa = tmem + L::TM_P + (n & 1) * 64;
+#pragma unroll
+        for (int kk = 0; kk < L::BN / 16; ++kk) {
+          const uint64_t vdesc = make_sdesc_sw128(v_addr + vs * L::TILE + kk * 16 * 128, L::BOX, 1024);
+          umma_ts(tmem + L::TM_O, pa + kk * 8, vdesc, idPV, (n > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&v_empty[vs]);
+        umma_commit(pv_done);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, g);
+      if (ok) ok = issue_S(0);
+      if (ok && N > 1) ok = issue_S(1);
+      for (int n = 0; ok && n < N; ++n) {
+        ok = issue_PV(n);
+        if (ok && n + 2 < N) ok = issue_S(n + 2);
+      }
+      // every MMA issued above must have finished before TMEM is released
+      umma_commit(mma_idle);
+      mbar_drain(mma_idle, 0, g.timeout_ns);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warps 0-3
+    const int t = threadIdx.x;  // row within the tile
+    const int row = m * L::BM + t;
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const float slope = load_slope(p.slopes, p.slopes_dtype, h);
+    const float c_sig = -p.sm_scale * kLog2e;
+    const float c_a = p.sm_scale * kLog2e;
+    const float slope2 = slope * kLog2e;
+    const int lim = p.causal ? min(row + 1, p.Skv) : p.Skv;
+    float m_ref = -INFINITY, l = 0.f, run = 0.f;
+    bool ok = true;
+    for (int n = 0; n < N; ++n) {
+      const int key0 = (last - n) * L::BN;
+      ok = mbar_wait(&s_full[n & 1], (n >> 1) & 1, g);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sreg[128];
+      const uint32_t sa = lane_base + L::TM_S + (n & 1) * 128;
+      tmem_ld32(sa, sreg);
+      tmem_ld32(sa + 32, sreg + 32);
+      tmem_ld32(sa + 64, sreg + 64);
+      tmem_ld32(sa + 96, sreg + 96);
+      tmem_ld_wait32(sreg);
+      tmem_ld_fence32(sreg + 32);
+      tmem_ld_fence32(sreg + 64);
+      tmem_ld_fence32(sreg + 96);
+
+      const bool masked = (key0 + L::BN > p.Skv) || (p.causal && key0 + L::BN - 1 > m * L::BM);
+      const float tmax = masked ? fwd_scan_tile<true>(sreg, run, key0, lim, c_sig, c_a, slope2)
+                                : fwd_scan_tile<false>(sreg, run, key0, lim, c_sig, c_a, slope2);
+      float alpha = 1.f;
+      bool resc = false;
+      if (m_ref == -INFINITY) {
+        m_ref = tmax;
+      } else if (tmax > m_ref + 8.f) {
+        alpha = ex2_approx(m_ref - tmax);
+        m_ref = tmax;
+        resc = true;
+      }
+      const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
+      uint32_t preg[64];
+      float ls0 = 0.f, ls1 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 64; ++j) {
+        const float e0 = ex2_approx(__uint_as_float(sreg[2 * j]) - m_use);
+        const float e1 = ex2_approx(__uint_as_float(sreg[2 * j + 1]) - m_use);
+        ls0 += e0;
+        ls1 += e1;
+        preg[j] = pack2<BF16>(e0, e1);
+      }
+      l = fmaf(l, alpha, ls0 + ls1);
+
+      if (n > 0) {
+        // O (and the P buffer written next) must be free of PV_{n-1}
+        ok = mbar_wait(pv_done, (n - 1) & 1, g);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+      }
+      if (__any_sync(0xffffffffu, resc)) {
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t oreg[32];
+          tmem_ld32(lane_base + L::TM_O + c * 32, oreg);
+          tmem_ld_wait32(oreg);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) oreg[j] = __float_as_uint(__uint_as_float(oreg[j]) * alpha);
+          tmem_st32(lane_base + L::TM_O + c * 32, oreg);
+        }
+      }
+      tmem_st32(lane_base + L::TM_P + (n & 1) * 64, preg);
+      tmem_st32(lane_base + L::TM_P + (n & 1) * 64 + 32, preg + 32);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&p_full[n & 1]);
+    }
+    if (ok) {
+      ok = mbar_wait(pv_done, (N - 1) & 1, g);
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (ok) {
+      tc_fence_after();
+      const float inv = 1.0f / (l + 1e-9f);
+      uint8_t* orow = static_cast<uint8_t*>(p.o) + ((size_t)bh * p.Sq + row) * D * 2;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t oreg[32];
+        tmem_ld32(lane_base + L::TM_O + c * 32, oreg);
+        tmem_ld_wait32(oreg);
+        if (row < p.Sq) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
+#pragma unroll
+          for (int v4 = 0; v4 < 4; ++v4) {
+            uint4 pk;
+            pk.x = pack2<BF16>(__uint_as_float(oreg[8 * v4 + 0]) * inv, __uint_as_float(oreg[8 * v4 + 1]) * inv);
+            pk.y = pack2<BF16>(__uint_as_float(oreg[8 * v4 + 2]) * inv, __uint_as_float(oreg[8 * v4 + 3]) * inv);
+            pk.z = pack2<BF16>(__uint_as_float(oreg[8 * v4 + 4]) * inv, __uint_as_float(oreg[8 * v4 + 5]) * inv);
+            pk.w = pack2<BF16>(__uint_as_float(oreg[8 * v4 + 6]) * inv, __uint_as_float(oreg[8 * v4 + 7]) * inv);
+            dst[v4] = pk;
+          }
+        }
+      }
+      if (row < p.Sq) {
+        const size_t ri = (size_t)bh * p.Sq + row;
+        p.lse[ri] = m_ref * kLn2 + logf(l + 1e-9f);
+        p.rowsig[ri] = run;
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TM_COLS);
+  }
+}
+
+}  // namespace coalibi

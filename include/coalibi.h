@@ -1,0 +1,132 @@
+/*
+ * coalibi.h -- C ABI of the sm_100a (B200) Co-ALiBi attention library
+ * (libcoalibi_sm100.so).
+ *
+ * Co-ALiBi attention, per batch b, query head h, query row i and key j:
+ *   p_ij = sm_scale * q_i . k_j          (masked where causal and j > i)
+ *   s_ij = sigmoid(p_ij), z_ij = sum_{t >= j} s_it
+ *   o_i  = softmax_j(p_ij - slope_h * z_ij) @ V
+ *
+ * All tensors are device pointers to contiguous row-major arrays:
+ *   q, o, dout, dq     [B, Hq,  Sq,  D]
+ *   k, v, dk, dv       [B, Hkv, Skv, D]      (Hq % Hkv == 0; q head h reads kv head h / (Hq/Hkv))
+ *   lse, rowsig        [B, Hq,  Sq]  float32
+ *   slopes             [Hq]          float32, float16 or bfloat16 (slopes_dtype)
+ * with D in {64, 128}, dtype float16 or bfloat16, every pointer 16-byte aligned.
+ *
+ * The library never allocates device memory, never synchronises and only
+ * enqueues work on the stream it is given (a cudaStream_t passed as void*; NULL
+ * means the legacy default stream).  Calls are reentrant and thread-safe across
+ * streams and devices.  Each function returns COALIBI_OK or an error code;
+ * coalibi_strerror() names it.  Kernel-side failures (a bounded wait that timed
+ * out) are reported asynchronously through the optional device status word.
+ */
+#ifndef COALIBI_H_
+#define COALIBI_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define COALIBI_ABI_VERSION 1
+
+enum coalibi_dtype {
+  COALIBI_F16 = 0,
+  COALIBI_BF16 = 1,
+  COALIBI_F32 = 2 /* only valid for slopes_dtype */
+};
+
+enum coalibi_error {
+  COALIBI_OK = 0,
+  COALIBI_ERR_NULL_POINTER = 1,
+  COALIBI_ERR_HEAD_DIM = 2,     /* D not in {64, 128} */
+  COALIBI_ERR_DTYPE = 3,        /* dtype not float16 / bfloat16 */
+  COALIBI_ERR_SHAPE = 4,        /* non-positive sizes, Hq % Hkv != 0, or too large */
+  COALIBI_ERR_ALIGNMENT = 5,    /* a pointer is not 16-byte aligned */
+  COALIBI_ERR_LAUNCH = 6,       /* CUDA launch / attribute error */
+  COALIBI_ERR_TENSOR_MAP = 7,   /* cuTensorMapEncodeTiled failed or unavailable */
+  COALIBI_ERR_WORKSPACE = 8,    /* workspace missing or smaller than coalibi_bwd_workspace_bytes() */
+  COALIBI_ERR_DEVICE = 9,       /* current device is not sm_100 */
+  COALIBI_ERR_TIMEOUT = 10      /* device status only: a bounded wait expired */
+};
+
+/* Forward.  Replaces the Triton launch in co_alibi_attn/co_alibi_attn.py:44-57
+ * (CoALIBIAttention.forward) and the kernel co_alibi_attn/co_alibi_fwd_kernel.py:29-127.
+ * Writes o, lse = m + log(l + 1e-9) (natural log) and rowsig = sum_j sigmoid(p_ij),
+ * the two float32 side outputs the backward consumes. */
+typedef struct CoalibiFwdArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* slopes;
+  void* o;
+  float* lse;
+  float* rowsig;
+  int B, Hq, Hkv, Sq, Skv, D;
+  int dtype;        /* enum coalibi_dtype of q, k, v, o */
+  int slopes_dtype; /* enum coalibi_dtype of slopes */
+  int causal;       /* nonzero: top-left aligned causal mask (key j > query i masked) */
+  float sm_scale;
+  int* status;      /* optional device int; a kernel-side error code is CAS'ed in */
+  unsigned int timeout_ms; /* bound on every in-kernel wait; 0 = default (2000 ms) */
+} CoalibiFwdArgs;
+
+int coalibi_fwd(const CoalibiFwdArgs* args, void* stream);
+
+/* Backward.  Replaces co_alibi_attn/co_alibi_attn.py:73-135 (CoALIBIAttention.backward,
+ * including the dk/dv partial-buffer reduction at :132-133 and, for GQA, the group
+ * sum autograd performs through repeat_interleave at :145-146) and the kernel
+ * co_alibi_attn/co_alibi_bwd_kernel.py:19-146.  dk and dv have Hkv heads.
+ * workspace: device scratch of at least coalibi_bwd_workspace_bytes() bytes,
+ * 256-byte aligned; its contents on entry do not matter. */
+typedef struct CoalibiBwdArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* o;
+  const void* dout;
+  const float* lse;
+  const float* rowsig;
+  const void* slopes;
+  void* dq;
+  void* dk;
+  void* dv;
+  void* workspace;
+  size_t workspace_bytes;
+  int B, Hq, Hkv, Sq, Skv, D;
+  int dtype;
+  int slopes_dtype;
+  int causal;
+  float sm_scale;
+  int* status;
+  unsigned int timeout_ms;
+} CoalibiBwdArgs;
+
+size_t coalibi_bwd_workspace_bytes(int B, int Hq, int Hkv, int Sq, int Skv, int D);
+
+int coalibi_bwd(const CoalibiBwdArgs* args, void* stream);
+
+/* Profiling aid with no counterpart in the reference: launch only the backward
+ * kernels selected by phase_mask (bit 0: delta = rowsum(dO * O) pre-pass, bit 1:
+ * pass A -> dq and the per-64-key carries in the workspace, bit 2: pass B -> dk, dv).
+ * Phases read what earlier phases wrote into the workspace, so they must run in
+ * order on one stream; coalibi_bwd(args, s) == coalibi_bwd_phases(args, 7, s). */
+int coalibi_bwd_phases(const CoalibiBwdArgs* args, int phase_mask, void* stream);
+
+/* Static name of an error code. */
+const char* coalibi_strerror(int code);
+
+/* COALIBI_ABI_VERSION of the loaded library. */
+int coalibi_abi_version(void);
+
+/* Detail (driver/runtime result and arguments) of the last failing call made by
+ * the calling thread; "" if none.  No counterpart in the reference. */
+const char* coalibi_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* COALIBI_H_ */

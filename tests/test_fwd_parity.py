@@ -1,0 +1,114 @@
+"""Forward parity: the sm_100a kernel through the public API against the CPU
+oracle on identical seeded inputs."""
+import glob
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from tests._common import make_inputs, oracle_fwd, oracle_fwd_pv, check_o, calc_sim
+
+pytestmark = pytest.mark.gpu
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+CASES = [
+    # B, Hq, Hkv, Sq, Skv, D, causal, dtype
+    (1, 2, 2, 128, 128, 128, True, torch.float16),
+    (1, 4, 4, 37, 37, 128, True, torch.float16),
+    (2, 3, 3, 255, 255, 64, True, torch.float16),
+    (1, 2, 2, 129, 129, 128, False, torch.bfloat16),
+    (1, 8, 2, 300, 300, 128, True, torch.bfloat16),
+    (1, 4, 1, 200, 200, 64, True, torch.float16),
+    (1, 2, 2, 16, 300, 128, True, torch.float16),
+    (1, 2, 2, 300, 16, 64, True, torch.float16),
+    (1, 3, 3, 384, 384, 64, False, torch.float16),
+    (2, 4, 4, 1024, 1024, 128, True, torch.float16),
+    (1, 12, 12, 513, 513, 64, True, torch.bfloat16),
+]
+
+
+def _ids(c):
+    B, Hq, Hkv, Sq, Skv, D, causal, dt = c
+    return f"B{B}H{Hq}-{Hkv}S{Sq}x{Skv}D{D}{'c' if causal else 'nc'}{'bf16' if dt == torch.bfloat16 else 'f16'}"
+
+
+@pytest.fixture(scope="module")
+def api():
+    import co_alibi_attn
+    return co_alibi_attn
+
+
+@pytest.mark.parametrize("case", CASES, ids=[_ids(c) for c in CASES])
+def test_forward_matches_oracle(api, case):
+    B, Hq, Hkv, Sq, Skv, D, causal, dtype = case
+    q, k, v, _ = make_inputs(B, Hq, Hkv, Sq, Skv, D, dtype, seed=Sq * 7 + D)
+    scale = 1.0 / math.sqrt(D)
+    o = api.co_alibi_attention(q.cuda(), k.cuda(), v.cuda(), causal=causal, sm_scale=scale)
+    torch.cuda.synchronize()
+    assert api.device_status(reset=True) == 0
+    o_ref, lse_ref, rs_ref, pv = oracle_fwd_pv(q, k, v, causal, scale)
+    ok, maxerr = check_o(o.cpu(), o_ref, dtype, pv)
+    assert ok, f"O max-abs error {maxerr:.3e}"
+    assert 1 - calc_sim(o.cpu(), o_ref) < 1e-4
+
+
+@pytest.mark.parametrize("case", CASES[:6], ids=[_ids(c) for c in CASES[:6]])
+def test_forward_side_outputs(api, case):
+    """lse and row_sig_total, the float32 tensors the backward consumes."""
+    from co_alibi_attn.co_alibi_attn import CoALIBIAttention, _api_slopes
+    B, Hq, Hkv, Sq, Skv, D, causal, dtype = case
+    q, k, v, _ = make_inputs(B, Hq, Hkv, Sq, Skv, D, dtype, seed=11)
+    scale = 1.0 / math.sqrt(D)
+    qc, kc, vc = q.cuda(), k.cuda(), v.cuda()
+    from co_alibi_attn.co_alibi_attn import _fwd
+    slopes = _api_slopes(Hq, 8.0, dtype, qc.device)
+    o, lse, rowsig = _fwd(qc, kc, vc, slopes, causal, scale)
+    torch.cuda.synchronize()
+    _, lse_ref, rs_ref = oracle_fwd(q, k, v, causal, scale)
+    assert (lse.cpu().double() - lse_ref).abs().max().item() < 2e-3
+    assert ((rowsig.cpu().double() - rs_ref).abs() / rs_ref.abs().clamp_min(1.0)).max().item() < 1e-4
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLD, "case_*.npz"))),
+                         ids=lambda p: os.path.basename(p)[5:-4])
+def test_forward_golden_fixtures(api, path):
+    """Reference-generated fixtures (small D) run through the kernel by zero-padding
+    D to 64, which leaves q.k, the outputs and the gradients' live columns unchanged."""
+    g = np.load(path)
+    q, k, v = (torch.from_numpy(g[n]) for n in ("q", "k", "v"))
+    D0 = q.shape[-1]
+    pad = lambda t: torch.nn.functional.pad(t, (0, 64 - D0)).to(torch.float16)
+    o = api.co_alibi_attention(pad(q).cuda(), pad(k).cuda(), pad(v).cuda(), causal=bool(g["causal"]),
+                               sm_scale=float(g["sm_scale"]), bias_max=float(g["bias_max"]))
+    o = o.cpu().double()
+    assert o[..., D0:].abs().max().item() == 0.0
+    # inputs were rounded to float16 on the way in, so compare at input-rounding scale
+    assert (o[..., :D0] - torch.from_numpy(g["o"])).abs().max().item() < 1e-2
+    # and tightly against the oracle on the rounded inputs
+    o_ref, _, _ = oracle_fwd(pad(q)[..., :D0], pad(k)[..., :D0], pad(v)[..., :D0], bool(g["causal"]),
+                             float(g["sm_scale"]), float(g["bias_max"]))
+    assert (o[..., :D0] - o_ref).abs().max().item() < 2e-3
+
+
+def test_forward_bench_shape_sampled(api):
+    """The README bench shape (B8 H16 S4096 D128 fp16 causal) on the GPU; the oracle
+    checks a sample of (b, h) slices in float32."""
+    from oracle import coalibi_oracle as orc
+    B, H, S, D = 8, 16, 4096, 128
+    q, k, v, _ = make_inputs(B, H, H, S, S, D, torch.float16, seed=0)
+    o = api.co_alibi_attention(q.cuda(), k.cuda(), v.cuda(), causal=True).cpu()
+    sl = orc.api_slopes(H, 8.0, torch.float16)
+    for (b, h) in [(0, 0), (3, 7), (7, 15)]:
+        ref = orc.forward_sliced(q, k, v, sl, True, None, torch.float32, units=[(b, h)])[(b, h)][0]
+        ok, err = check_o(o[b, h], ref, torch.float16)
+        assert ok, f"(b={b}, h={h}) O max-abs {err:.3e}"
+
+
+def test_forward_deterministic(api):
+    q, k, v, _ = make_inputs(1, 4, 4, 700, 700, 128, torch.float16, seed=5)
+    a = api.co_alibi_attention(q.cuda(), k.cuda(), v.cuda())
+    b = api.co_alibi_attention(q.cuda(), k.cuda(), v.cuda())
+    assert torch.equal(a, b)
