@@ -39,8 +39,10 @@ class CoalibiBwdArgs(ctypes.Structure):
     ]
 
 
-EXPORTS = ("coalibi_fwd", "coalibi_bwd", "coalibi_bwd_phases", "coalibi_bwd_workspace_bytes",
-           "coalibi_strerror", "coalibi_abi_version", "coalibi_last_error")
+EXPORTS = ("coalibi_fwd", "coalibi_bwd", "coalibi_bwd_phases", "coalibi_bwd_noalloc",
+           "coalibi_bwd_workspace_bytes", "coalibi_strerror", "coalibi_abi_version", "coalibi_last_error")
+
+NOALLOC_SCRATCH_BYTES = 64 << 20  # COALIBI_NOALLOC_SCRATCH_BYTES
 
 _lock = threading.Lock()
 _lib = None
@@ -64,6 +66,8 @@ def load():
             lib.coalibi_bwd.restype = c_int
             lib.coalibi_bwd_phases.argtypes = [ctypes.POINTER(CoalibiBwdArgs), c_int, c_void_p]
             lib.coalibi_bwd_phases.restype = c_int
+            lib.coalibi_bwd_noalloc.argtypes = [ctypes.POINTER(CoalibiBwdArgs), c_void_p]
+            lib.coalibi_bwd_noalloc.restype = c_int
             lib.coalibi_bwd_workspace_bytes.argtypes = [c_int] * 6
             lib.coalibi_bwd_workspace_bytes.restype = c_size_t
             lib.coalibi_strerror.argtypes = [c_int]

@@ -19,6 +19,8 @@ namespace coalibi {
 // Human-readable detail of the last failure on this thread (coalibi_last_error()).
 static thread_local char g_last_error[256] = "";
 
+void set_last_error_detail(const char* msg) { snprintf(g_last_error, sizeof(g_last_error), "%s", msg); }
+
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;

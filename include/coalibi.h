@@ -115,6 +115,22 @@ int coalibi_bwd(const CoalibiBwdArgs* args, void* stream);
  * order on one stream; coalibi_bwd(args, s) == coalibi_bwd_phases(args, 7, s). */
 int coalibi_bwd_phases(const CoalibiBwdArgs* args, int phase_mask, void* stream);
 
+/* Size of the static device scratch used by coalibi_bwd_noalloc (64 MiB). */
+#define COALIBI_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
+
+/* Backward that allocates nothing and needs no workspace: same arguments and
+ * results as coalibi_bwd, with args->workspace / workspace_bytes ignored.  It has
+ * no counterpart in the reference.  It is for callers that cannot allocate device
+ * memory at the call -- a plugin host or FFI caller that owns only the tensors
+ * it passes, or code that must avoid cudaMalloc there because it can synchronise
+ * the device.  Its scratch is one file-scope device array of
+ * COALIBI_NOALLOC_SCRATCH_BYTES per GPU, held until the process exits; problems
+ * needing more (coalibi_bwd_workspace_bytes() > that) return COALIBI_ERR_WORKSPACE
+ * without launching.  The first call on each device looks up the array's device
+ * address (cudaGetSymbolAddress); make it before any stream capture.  All calls on
+ * a device share the array, so calls that overlap on the GPU race: serialise them. */
+int coalibi_bwd_noalloc(const CoalibiBwdArgs* args, void* stream);
+
 /* Static name of an error code. */
 const char* coalibi_strerror(int code);
 
