@@ -197,7 +197,7 @@ def metric_name(config):
 
 def config_dict(args, cfg):
     B, Hq, Hkv, S, D, dtype, causal, std, fwd_only = cfg
-    per_rank_B = B if args.scaling == "weak" else B
+    per_rank_B = B if args.scaling == "weak" else max(1, B // args.gpus)
     return {"workload": f"{args.config}: co_alibi_attention {'fwd' if fwd_only else 'fwd+bwd'} B={B} Hq={Hq} "
                         f"Hkv={Hkv} S={S} D={D} {str(dtype).split('.')[-1]} "
                         f"{'causal' if causal else 'non-causal'}",
@@ -219,10 +219,14 @@ def main():
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
     ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the config's batch size (small cases for ncu captures)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     cfg = CONFIGS[args.config]
+    if args.batch:
+        cfg = (args.batch,) + cfg[1:]
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -243,15 +247,19 @@ def main():
     from co_alibi_attn import co_alibi_attention
     import co_alibi_attn.co_alibi_attn as impl
 
+    from co_alibi_attn.sharding import shard_plan, sharded_attention
     B, Hq, Hkv, S, D, dtype, causal, std, fwd_only = cfg
     if args.scaling == "strong" and world > 1:
-        # split the batch's B*Hkv units; each rank keeps whole batch rows when possible
-        assert B % world == 0 or (B * Hkv) % world == 0
-        B_r = B // world if B % world == 0 else B
-        Hkv_r = Hkv if B % world == 0 else Hkv // world
-        Hq_r = Hq if B % world == 0 else Hq // world
+        # the batch's B*Hkv (b, kv head) units split into one contiguous block per rank
+        shard = shard_plan(B, Hq, Hkv, world, rank)
     else:
-        B_r, Hq_r, Hkv_r = B, Hq, Hkv
+        shard = shard_plan(B, Hq, Hkv, 1, 0)
+    B_r, Hq_r, Hkv_r = shard.b1 - shard.b0, shard.h1 - shard.h0, shard.g1 - shard.g0
+
+    def attn(q_, k_, v_):
+        if args.scaling == "strong" and world > 1:
+            return sharded_attention(q_, k_, v_, shard, Hq, causal=causal)
+        return co_alibi_attention(q_, k_, v_, causal=causal)
 
     g = torch.Generator().manual_seed(1000 + rank)
     q_h = (torch.randn(B_r, Hq_r, S, D, generator=g) * std).to(dtype).pin_memory()
@@ -271,9 +279,9 @@ def main():
     def step():
         if fwd_only:
             with torch.no_grad():
-                co_alibi_attention(q, k, v, causal=causal)
+                attn(q, k, v)
         else:
-            o = co_alibi_attention(q, k, v, causal=causal)
+            o = attn(q, k, v)
             o.backward(do)
             q.grad = k.grad = v.grad = None
 
@@ -333,11 +341,11 @@ def main():
                 dod.copy_(do_h, non_blocking=True)
         if fwd_only:
             with torch.no_grad():
-                o = co_alibi_attention(qd, kd, vd, causal=causal)
+                o = attn(qd, kd, vd)
             outs_h[0].copy_(o, non_blocking=True)
         else:
             qd.requires_grad_(True), kd.requires_grad_(True), vd.requires_grad_(True)
-            o = co_alibi_attention(qd, kd, vd, causal=causal)
+            o = attn(qd, kd, vd)
             o.backward(dod)
             outs_h[0].copy_(o.detach(), non_blocking=True)
             outs_h[1].copy_(qd.grad, non_blocking=True)
@@ -346,16 +354,18 @@ def main():
             qd.grad = kd.grad = vd.grad = None
             qd.requires_grad_(False), kd.requires_grad_(False), vd.requires_grad_(False)
 
-    e2e_step()
-    torch.cuda.synchronize()
-    barrier()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record()
-    for _ in range(args.e2e_steps):
+    e2e_ms = float("nan")
+    if args.e2e_steps > 0:
         e2e_step()
-    f1.record()
-    torch.cuda.synchronize()
-    e2e_ms = f0.elapsed_time(f1) / args.e2e_steps
+        torch.cuda.synchronize()
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        f1.record()
+        torch.cuda.synchronize()
+        e2e_ms = f0.elapsed_time(f1) / args.e2e_steps
     t = torch.tensor([e2e_ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

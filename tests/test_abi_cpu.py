@@ -1,0 +1,99 @@
+"""C ABI and host logic without a GPU: the library loads on a CPU-only host,
+exports every function include/coalibi.h declares, validates arguments before
+touching a device, and the Python layer keeps the reference's error behaviour."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _header_functions():
+    txt = open(os.path.join(ROOT, "include", "coalibi.h")).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[a-z_]+\**\s+\**(coalibi_[a-z_0-9]+)\s*\(", txt, re.M)))
+
+
+def test_library_exports_every_header_function():
+    from co_alibi_attn import _lib
+    lib = _lib.load()
+    names = _header_functions()
+    assert "coalibi_fwd" in names and "coalibi_bwd_noalloc" in names
+    for n in names:
+        assert hasattr(lib, n), n
+    assert sorted(_lib.EXPORTS) == names
+    assert lib.coalibi_abi_version() == 1
+
+
+def test_strerror_and_workspace_size():
+    from co_alibi_attn import _lib
+    lib = _lib.load()
+    for code in range(0, 11):
+        assert _lib.strerror(code)
+    assert "head dim" in _lib.strerror(2)
+    sq_pad, nkb = 4096, 64
+    want = 8 * 16 * sq_pad * 4 + 8 * 16 * nkb * sq_pad * 8
+    assert lib.coalibi_bwd_workspace_bytes(8, 16, 16, 4096, 4096, 128) == want
+    assert lib.coalibi_bwd_workspace_bytes(1, 4, 4, 37, 37, 64) == 256 * ((4 * 128 * 4 + 255) // 256) + \
+        256 * ((4 * 1 * 128 * 8 + 255) // 256)
+    assert lib.coalibi_bwd_workspace_bytes(0, 4, 4, 37, 37, 64) == 0
+
+
+def _fwd_args(_lib, **kw):
+    base = dict(q=16, k=16, v=16, slopes=16, o=16, lse=16, rowsig=16, B=1, Hq=2, Hkv=2, Sq=8, Skv=8, D=128,
+                dtype=0, slopes_dtype=0, causal=1, sm_scale=0.1, status=None, timeout_ms=0)
+    base.update(kw)
+    return _lib.CoalibiFwdArgs(**base)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(D=96), 2), (dict(dtype=2), 3), (dict(slopes_dtype=7), 3), (dict(Hkv=3, Hq=4), 4),
+    (dict(B=0), 4), (dict(q=None), 1), (dict(q=24), 5),
+])
+def test_fwd_argument_validation_happens_before_device_use(kw, code):
+    from co_alibi_attn import _lib
+    lib = _lib.load()
+    assert lib.coalibi_fwd(ctypes.byref(_fwd_args(_lib, **kw)), None) == code
+    assert lib.coalibi_fwd(None, None) == 1
+
+
+def test_bwd_validation_and_phase_mask():
+    from co_alibi_attn import _lib
+    lib = _lib.load()
+    a = _lib.CoalibiBwdArgs(q=16, k=16, v=16, o=16, dout=16, lse=16, rowsig=16, slopes=16, dq=16, dk=16,
+                            dv=16, workspace=None, workspace_bytes=0, B=1, Hq=2, Hkv=2, Sq=8, Skv=8, D=64,
+                            dtype=0, slopes_dtype=0, causal=1, sm_scale=0.1, status=None, timeout_ms=0)
+    assert lib.coalibi_bwd(ctypes.byref(a), None) == 8          # no workspace
+    assert lib.coalibi_bwd_phases(ctypes.byref(a), 8, None) == 4  # bad phase mask
+    a.workspace, a.workspace_bytes = 256 + 16, 1 << 20
+    assert lib.coalibi_bwd(ctypes.byref(a), None) == 5          # workspace not 256-aligned
+    big = _lib.CoalibiBwdArgs(**{f: getattr(a, f) for f, _ in _lib.CoalibiBwdArgs._fields_})
+    big.B, big.Hq, big.Hkv, big.Sq, big.Skv, big.D = 8, 16, 16, 4096, 4096, 128
+    assert lib.coalibi_bwd_noalloc(ctypes.byref(big), None) == 8  # exceeds the static scratch
+    assert "static scratch" in lib.coalibi_last_error().decode()
+
+
+def test_slope_table_matches_reference_fixture():
+    import numpy as np
+    from co_alibi_attn.co_alibi_attn import _get_coalibi_slopes
+    tabs = np.load(os.path.join(ROOT, "tests", "golden", "slopes.npz"))
+    for h in (1, 3, 4, 12, 16, 32, 48, 64):
+        for bm in (2.5, 4.0, 8.0, 16.0):
+            assert np.array_equal(_get_coalibi_slopes(h, bm).float().numpy(), tabs[f"bm{bm}_h{h}"])
+
+
+def test_python_layer_rejects_cpu_tensors_like_the_reference():
+    from co_alibi_attn import co_alibi_attention
+    q = torch.randn(1, 2, 8, 64, dtype=torch.float16)
+    with pytest.raises(AssertionError):
+        co_alibi_attention(q, q, q)
+
+
+def test_sharded_api_slopes_are_global():
+    from co_alibi_attn.sharding import shard_plan, shard_slopes
+    from co_alibi_attn.co_alibi_attn import _get_coalibi_slopes
+    sh = shard_plan(4, 32, 8, 8, 5)
+    s = shard_slopes(32, sh, 8.0, torch.float32, "cpu")
+    assert torch.equal(s, (2.0 * _get_coalibi_slopes(32, 8.0))[20:24].float())
