@@ -41,9 +41,10 @@ CONFIGS = {
     "cfg4": (16, 12, 12, 2048, 64, torch.float16, False, 0.5, True),
 }
 
-# Per-launch DRAM traffic (read + write bytes) of each kernel at cfg2 from one
-# ncu capture (profiles/ncu_cfg2_*.txt); None where not captured yet.
-NCU_TRAFFIC_CFG2 = {"fwd": None, "bwd_a": None, "bwd_b": None, "bwd_delta": None}
+# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of each
+# kernel at cfg2: one ncu capture at B=2 (profiles/<kernel>_kernel_cfg2_b2_ncu_full.txt)
+# scaled by 4 to the B=8 launch (traffic grows with the number of (b, h) units).
+NCU_TRAFFIC_CFG2 = {"fwd": 4 * 116.226e6, "bwd_a": 4 * 179.122e6, "bwd_b": 4 * 216.989e6, "bwd_delta": None}
 
 
 def visible(S, causal):
