@@ -147,36 +147,42 @@ __device__ __forceinline__ void bwd_chunk(const uint32_t* sreg, const uint32_t* 
 
 // ---------------------------------------------------------------------------
 // 2. pass A: dQ and the per-64-key carries
+//
+// Two 128-row query tiles ("slots") per CTA on two softmax warpgroups; key
+// sub-tiles of 64, left to right.  TMEM per slot s (column 256*s): S [0,64)
+// with dP aliased over its first 32 columns once read, dS [64,128), dQ [128,128+D).
 // ---------------------------------------------------------------------------
 template <int D>
 struct BwdALayout {
-  static constexpr int BM = 128, BN = 128;
-  static constexpr int KS = 2, VS = 2;
-  static constexpr int BOX = 128 * 128;
-  static constexpr int TILE = BN * D * 2;
+  static constexpr int BM = 128, BN = 64;
+  static constexpr int KS = 3, VS = 2;
+  static constexpr int QBOX = 128 * 128;   // [128 rows][64 cols] box
+  static constexpr int KBOX = BN * 128;    // [64 rows][64 cols] box
+  static constexpr int TILE = BN * D * 2;  // one 64-key K or V sub-tile
   static constexpr int QB = BM * D * 2;
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_DO = QB;
-  static constexpr int OFF_K = 2 * QB;
+  static constexpr int OFF_Q = 0;          // Q slot 0, Q slot 1, dO slot 0, dO slot 1
+  static constexpr int OFF_K = 4 * QB;
   static constexpr int OFF_V = OFF_K + KS * TILE;
   static constexpr int OFF_BAR = OFF_V + VS * TILE;
-  static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 1 + 1 + 2 + 1 + 1;
+  static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 2 + 2 + 2 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 16;
   static constexpr int ALLOC = BYTES + 1024;
-  static constexpr uint32_t TM_S = 0, TM_DS = 128, TM_DQ = 256, TM_DP = 256 + D, TM_COLS = 512;
+  static constexpr int THREADS = 320;      // 2 softmax warpgroups + TMA warp + MMA warp
+  static constexpr int WARP_TMA = 8, WARP_MMA = 9;
+  static constexpr uint32_t TM_SLOT = 256, TM_S = 0, TM_DS = 64, TM_DQ = 128, TM_COLS = 512;
+  static_assert(ALLOC <= 232448, "shared memory budget");
 };
 
 template <int D, bool BF16>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     coalibi_bwd_a_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
                          const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                          const BwdParams p) {
   using L = BwdALayout<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem + L::OFF_Q;
-  uint8_t* sDO = smem + L::OFF_DO;
+  uint8_t* sQ = smem + L::OFF_Q;  // slot s: Q at s*QB, dO at (2+s)*QB
   uint8_t* sK = smem + L::OFF_K;
   uint8_t* sV = smem + L::OFF_V;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
@@ -185,24 +191,28 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* k_empty = k_full + L::KS;
   uint64_t* v_full = k_empty + L::KS;
   uint64_t* v_empty = v_full + L::VS;
-  uint64_t* s_full = v_empty + L::VS;
-  uint64_t* s_free = s_full + 1;
-  uint64_t* dp_full = s_free + 1;
-  uint64_t* dq_done = dp_full + 2;
-  uint64_t* mma_idle = dq_done + 1;
+  uint64_t* s_full = v_empty + L::VS;  // [2]
+  uint64_t* dp_full = s_full + 2;      // [2]
+  uint64_t* dq_done = dp_full + 2;     // [2]
+  uint64_t* mma_idle = dq_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
   const int warp = warp_id();
   const int lane = lane_id();
   const int BH = p.B * p.Hq;
-  int bh, m;
-  decode_tile(blockIdx.x, BH, p.n_qtiles, bh, m);
+  const int n_pairs = (p.n_qtiles + 1) / 2;
+  int bh, pair;
+  decode_tile(blockIdx.x, BH, n_pairs, bh, pair);
   const int b = bh / p.Hq;
   const int h = bh - b * p.Hq;
   const int zkv = b * p.Hkv + h / (p.Hq / p.Hkv);
-  const int last = p.causal ? min(p.n_kvtiles - 1, (m * L::BM + L::BM - 1) / L::BN) : p.n_kvtiles - 1;
-  const int T = last + 1;
+  const bool has1 = (2 * pair + 1) < p.n_qtiles;
+  // last 64-key sub-tile each slot visits (causal: sub-tiles starting at or before its last row)
+  const int last0 = p.causal ? min(p.n_kb64 - 1, (2 * pair) * 2 + 1) : p.n_kb64 - 1;
+  const int last1 = has1 ? (p.causal ? min(p.n_kb64 - 1, (2 * pair + 1) * 2 + 1) : p.n_kb64 - 1) : -1;
+  const int N = max(last0, last1) + 1;
+  auto active = [&](int s, int n) -> bool { return n <= (s == 0 ? last0 : last1); };
   CtaGuard g{abort_flag, p.status, p.timeout_ns};
 
   if (threadIdx.x == 0) {
@@ -215,16 +225,16 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(s_free, 128);
-    mbar_init(&dp_full[0], 128);
-    mbar_init(&dp_full[1], 128);
-    mbar_init(dq_done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&dp_full[i], 128);
+      mbar_init(&dq_done[i], 1);
+    }
     mbar_init(mma_idle, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == L::WARP_MMA) {
     tmem_alloc(tmem_slot, L::TM_COLS);
     tmem_relinquish();
   }
@@ -233,33 +243,35 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == L::WARP_TMA) {
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmDO);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(q_full, 2 * L::QB);
+      const int nslots = has1 ? 2 : 1;
+      mbar_arrive_expect_tx(q_full, 2 * nslots * L::QB);
+      for (int s = 0; s < nslots; ++s)
 #pragma unroll
-      for (int bx = 0; bx < D / 64; ++bx) {
-        tma_load_3d(sQ + bx * L::BOX, &tmQ, q_full, bx * 64, m * L::BM, bh);
-        tma_load_3d(sDO + bx * L::BOX, &tmDO, q_full, bx * 64, m * L::BM, bh);
-      }
+        for (int bx = 0; bx < D / 64; ++bx) {
+          tma_load_3d(sQ + s * L::QB + bx * L::QBOX, &tmQ, q_full, bx * 64, (2 * pair + s) * L::BM, bh);
+          tma_load_3d(sQ + (2 + s) * L::QB + bx * L::QBOX, &tmDO, q_full, bx * 64, (2 * pair + s) * L::BM, bh);
+        }
       int nk = 0, nv = 0;
-      for (int t = 0; t < T; ++t) {
-        const int ks = t % L::KS;
-        if (!mbar_wait(&k_empty[ks], ((t / L::KS) & 1) ^ 1, g)) break;
+      for (int n = 0; n < N; ++n) {
+        const int ks = n % L::KS;
+        if (!mbar_wait(&k_empty[ks], ((n / L::KS) & 1) ^ 1, g)) break;
         mbar_arrive_expect_tx(&k_full[ks], L::TILE);
 #pragma unroll
         for (int bx = 0; bx < D / 64; ++bx)
-          tma_load_3d(sK + ks * L::TILE + bx * L::BOX, &tmK, &k_full[ks], bx * 64, t * L::BN, zkv);
+          tma_load_3d(sK + ks * L::TILE + bx * L::KBOX, &tmK, &k_full[ks], bx * 64, n * L::BN, zkv);
         ++nk;
-        const int vs = t % L::VS;
-        if (!mbar_wait(&v_empty[vs], ((t / L::VS) & 1) ^ 1, g)) break;
+        const int vs = n % L::VS;
+        if (!mbar_wait(&v_empty[vs], ((n / L::VS) & 1) ^ 1, g)) break;
         mbar_arrive_expect_tx(&v_full[vs], L::TILE);
 #pragma unroll
         for (int bx = 0; bx < D / 64; ++bx)
-          tma_load_3d(sV + vs * L::TILE + bx * L::BOX, &tmV, &v_full[vs], bx * 64, t * L::BN, zkv);
+          tma_load_3d(sV + vs * L::TILE + bx * L::KBOX, &tmV, &v_full[vs], bx * 64, n * L::BN, zkv);
         ++nv;
       }
       mbar_drain(q_full, 0, g.timeout_ns);
@@ -272,59 +284,84 @@ __global__ void __launch_bounds__(192, 1)
         if (uses > 0) mbar_drain(&v_full[s], (uses - 1) & 1, g.timeout_ns);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == L::WARP_MMA) {
     if (lane == 0) {
       constexpr uint32_t idS = make_idesc_f16(BF16, 128, L::BN, false, false);
       constexpr uint32_t idQ = make_idesc_f16(BF16, 128, D, false, true);
-      const uint32_t q_addr = smem_u32(sQ), do_addr = smem_u32(sDO);
+      const uint32_t q_addr = smem_u32(sQ);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-      auto issue_SdS = [&](int t) -> bool {
-        const int ks = t % L::KS, vs = t % L::VS;
-        if (!mbar_wait(&k_full[ks], (t / L::KS) & 1, g)) return false;
-        if (!mbar_wait(&v_full[vs], (t / L::VS) & 1, g)) return false;
+      int kv_waited = -1;
+      int dq_cnt[2] = {0, 0};
+      auto wait_kv = [&](int n) -> bool {
+        if (kv_waited >= n) return true;
+        kv_waited = n;
+        if (!mbar_wait(&k_full[n % L::KS], (n / L::KS) & 1, g)) return false;
+        if (!mbar_wait(&v_full[n % L::VS], (n / L::VS) & 1, g)) return false;
         tc_fence_after();
+        return true;
+      };
+      // S_s = Q_s K_n^T and dS_s = dO_s V_n^T (64 key columns each)
+      auto issue_SdS = [&](int s, int n) -> bool {
+        if (!wait_kv(n)) return false;
+        const int ks = n % L::KS, vs = n % L::VS;
+        const uint32_t qa = q_addr + s * L::QB, da = q_addr + (2 + s) * L::QB;
+        const uint32_t base = tmem + s * L::TM_SLOT;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * L::BOX + (kk & 3) * 32;
-          umma_ss(tmem + L::TM_S, make_sdesc_sw128(q_addr + off, 16, 1024),
-                  make_sdesc_sw128(k_addr + ks * L::TILE + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
+          const uint32_t qo = (kk >> 2) * L::QBOX + (kk & 3) * 32;
+          const uint32_t ko = (kk >> 2) * L::KBOX + (kk & 3) * 32;
+          umma_ss(base + L::TM_S, make_sdesc_sw128(qa + qo, 16, 1024),
+                  make_sdesc_sw128(k_addr + ks * L::TILE + ko, 16, 1024), idS, kk > 0 ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * L::BOX + (kk & 3) * 32;
-          umma_ss(tmem + L::TM_DS, make_sdesc_sw128(do_addr + off, 16, 1024),
-                  make_sdesc_sw128(v_addr + vs * L::TILE + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
+          const uint32_t qo = (kk >> 2) * L::QBOX + (kk & 3) * 32;
+          const uint32_t ko = (kk >> 2) * L::KBOX + (kk & 3) * 32;
+          umma_ss(base + L::TM_DS, make_sdesc_sw128(da + qo, 16, 1024),
+                  make_sdesc_sw128(v_addr + vs * L::TILE + ko, 16, 1024), idS, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&v_empty[vs]);
-        umma_commit(s_full);
+        umma_commit(&s_full[s]);
+        if (s == 1 || !active(1, n)) umma_commit(&v_empty[vs]);  // V_n only feeds dS
         return true;
       };
       bool ok = mbar_wait(q_full, 0, g);
-      if (ok) ok = issue_SdS(0);
-      for (int t = 0; ok && t < T; ++t) {
-        ok = mbar_wait(s_free, t & 1, g);
-        if (ok && t + 1 < T) ok = issue_SdS(t + 1);
-        if (ok) ok = mbar_wait(&dp_full[t & 1], (t >> 1) & 1, g);
-        if (!ok) break;
-        tc_fence_after();
-        const int ks = t % L::KS;
-        const uint32_t pa = tmem + L::TM_DP + (t & 1) * 64;
+      for (int s = 0; ok && s < 2; ++s)
+        if (active(s, 0)) ok = issue_SdS(s, 0);
+      for (int n = 0; ok && n < N; ++n) {
+        for (int s = 0; ok && s < 2; ++s) {
+          const bool act = active(s, n);
+          if (act) {
+            if (!(ok = mbar_wait(&dp_full[s], dq_cnt[s] & 1, g))) break;
+            tc_fence_after();
+            const int ks = n % L::KS;
+            const uint32_t base = tmem + s * L::TM_SLOT;
 #pragma unroll
-        for (int kk = 0; kk < L::BN / 16; ++kk) {
-          const uint64_t kdesc = make_sdesc_sw128(k_addr + ks * L::TILE + kk * 16 * 128, L::BOX, 1024);
-          umma_ts(tmem + L::TM_DQ, pa + kk * 8, kdesc, idQ, (t > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < L::BN / 16; ++kk) {
+              // A = dP (TMEM, aliased over S), B = K_n as (N = d, K = keys): MN-major, 64-d blocks one box apart
+              const uint64_t kdesc = make_sdesc_sw128(k_addr + ks * L::TILE + kk * 16 * 128, L::KBOX, 1024);
+              umma_ts(base + L::TM_DQ, base + L::TM_S + kk * 8, kdesc, idQ, (dq_cnt[s] > 0 || kk > 0) ? 1u : 0u);
+            }
+            umma_commit(&dq_done[s]);
+            if (s == 1 || !active(1, n)) umma_commit(&k_empty[ks]);
+            ++dq_cnt[s];
+          }
+          if (n + 1 < N && active(s, n + 1)) {
+            // S_s(n+1) overwrites the columns dP_s(n) is read from
+            if (act && !(ok = mbar_wait(&dq_done[s], (dq_cnt[s] - 1) & 1, g))) break;
+            ok = issue_SdS(s, n + 1);
+          }
         }
-        umma_commit(&k_empty[ks]);
       }
-      if (ok) umma_commit(dq_done);
       umma_commit(mma_idle);
       mbar_drain(mma_idle, 0, g.timeout_ns);
     }
-  } else {
-    const int t_row = threadIdx.x;
-    const int row = m * L::BM + t_row;
+  } else if (warp < 8) {
+    const int slot = warp >> 2;
+    const int t_row = threadIdx.x & 127;
+    const int qt = 2 * pair + slot;
+    const int row = qt * L::BM + t_row;
     const bool row_ok = row < p.Sq;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t lane_base = tmem + slot * L::TM_SLOT + ((uint32_t)((warp & 3) * 32) << 16);
     const float slope = load_slope(p.slopes, p.slopes_dtype, h);
     const float c_sig = -p.sm_scale * kLog2e;
     const float c_a = p.sm_scale * kLog2e;
@@ -334,69 +371,67 @@ __global__ void __launch_bounds__(192, 1)
     float zs = row_ok ? p.rowsig[ri] : 0.f;
     const float delta = p.delta[(size_t)bh * p.sq_pad + row];
     const int lim = row_ok ? (p.causal ? min(row + 1, p.Skv) : p.Skv) : 0;
-    const bool rows_partial = (m * L::BM + L::BM > p.Sq);
+    const bool rows_partial = (qt * L::BM + L::BM > p.Sq);
     float cacc = 0.f;
     float2* carry_row = p.carry + (size_t)bh * p.n_kb64 * p.sq_pad + row;
     bool ok = true;
-    for (int t = 0; t < T; ++t) {
-      const int key0 = t * L::BN;
-      ok = mbar_wait(s_full, t & 1, g);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      tc_fence_after();
-      const bool masked =
-          rows_partial || (key0 + L::BN > p.Skv) || (p.causal && key0 + L::BN - 1 > m * L::BM);
-      const uint32_t dpa = lane_base + L::TM_DP + (t & 1) * 64;
+    int it = 0;
+    if (slot == 0 || has1) {
+      for (int n = 0; n < N; ++n) {
+        if (!active(slot, n)) break;  // activity is a prefix of the sweep
+        const int key0 = n * L::BN;
+        ok = mbar_wait(&s_full[slot], it & 1, g);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        carry_row[(size_t)n * p.sq_pad] = make_float2(zs, cacc);
+        const bool masked =
+            rows_partial || (key0 + L::BN > p.Skv) || (p.causal && key0 + L::BN - 1 > qt * L::BM);
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sreg[32], dsreg[32];
-        tmem_ld32(lane_base + L::TM_S + c * 32, sreg);
-        tmem_ld32(lane_base + L::TM_DS + c * 32, dsreg);
-        tmem_ld_wait32(sreg);
-        tmem_ld_fence32(dsreg);
-        if (c == 3) {
-          tc_fence_before();
-          mbar_arrive(s_free);
+        for (int c = 0; c < 2; ++c) {
+          uint32_t sreg[32], dsreg[32];
+          tmem_ld32(lane_base + L::TM_S + c * 32, sreg);
+          tmem_ld32(lane_base + L::TM_DS + c * 32, dsreg);
+          tmem_ld_wait32(sreg);
+          tmem_ld_fence32(dsreg);
+          uint32_t dpo[16];
+          if (masked)
+            bwd_chunk<true, BF16, false>(sreg, dsreg, key0 + c * 32, lim, c_sig, c_a, slope, slope2, lse2, delta,
+                                         zs, cacc, dpo, nullptr);
+          else
+            bwd_chunk<false, BF16, false>(sreg, dsreg, key0 + c * 32, lim, c_sig, c_a, slope, slope2, lse2,
+                                          delta, zs, cacc, dpo, nullptr);
+          tmem_st16(lane_base + L::TM_S + c * 16, dpo);  // over S columns already read
         }
-        if ((c & 1) == 0) {
-          const int kb = 2 * t + (c >> 1);
-          if (kb < p.n_kb64) carry_row[(size_t)kb * p.sq_pad] = make_float2(zs, cacc);
-        }
-        uint32_t dpo[16];
-        if (masked)
-          bwd_chunk<true, BF16, false>(sreg, dsreg, key0 + c * 32, lim, c_sig, c_a, slope, slope2, lse2, delta,
-                                       zs, cacc, dpo, nullptr);
-        else
-          bwd_chunk<false, BF16, false>(sreg, dsreg, key0 + c * 32, lim, c_sig, c_a, slope, slope2, lse2,
-                                        delta, zs, cacc, dpo, nullptr);
-        tmem_st16(dpa + c * 16, dpo);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&dp_full[slot]);
+        ++it;
       }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&dp_full[t & 1]);
-    }
-    if (ok) {
-      ok = mbar_wait(dq_done, 0, g);
-      ok = __all_sync(0xffffffffu, ok);
-    }
-    if (ok) {
-      tc_fence_after();
-      uint8_t* dst_row = static_cast<uint8_t*>(p.dq) + ri * D * 2;
+      if (ok && it > 0) {
+        ok = mbar_wait(&dq_done[slot], (it - 1) & 1, g);
+        ok = __all_sync(0xffffffffu, ok);
+      }
+      if (ok && it > 0) {
+        tc_fence_after();
+        uint8_t* dst_row = static_cast<uint8_t*>(p.dq) + ri * D * 2;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(lane_base + L::TM_DQ + c * 32, r);
-        tmem_ld_wait32(r);
-        if (row_ok) {
-          uint4* dst = reinterpret_cast<uint4*>(dst_row + c * 64);
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(lane_base + L::TM_DQ + c * 32, r);
+          tmem_ld_wait32(r);
+          if (row_ok) {
+            uint4* dst = reinterpret_cast<uint4*>(dst_row + c * 64);
+            const float sc = p.sm_scale;
 #pragma unroll
-          for (int v4 = 0; v4 < 4; ++v4) {
-            uint4 pk;
-            pk.x = pack2<BF16>(__uint_as_float(r[8 * v4 + 0]) * p.sm_scale, __uint_as_float(r[8 * v4 + 1]) * p.sm_scale);
-            pk.y = pack2<BF16>(__uint_as_float(r[8 * v4 + 2]) * p.sm_scale, __uint_as_float(r[8 * v4 + 3]) * p.sm_scale);
-            pk.z = pack2<BF16>(__uint_as_float(r[8 * v4 + 4]) * p.sm_scale, __uint_as_float(r[8 * v4 + 5]) * p.sm_scale);
-            pk.w = pack2<BF16>(__uint_as_float(r[8 * v4 + 6]) * p.sm_scale, __uint_as_float(r[8 * v4 + 7]) * p.sm_scale);
-            dst[v4] = pk;
+            for (int v4 = 0; v4 < 4; ++v4) {
+              uint4 pk;
+              pk.x = pack2<BF16>(__uint_as_float(r[8 * v4 + 0]) * sc, __uint_as_float(r[8 * v4 + 1]) * sc);
+              pk.y = pack2<BF16>(__uint_as_float(r[8 * v4 + 2]) * sc, __uint_as_float(r[8 * v4 + 3]) * sc);
+              pk.z = pack2<BF16>(__uint_as_float(r[8 * v4 + 4]) * sc, __uint_as_float(r[8 * v4 + 5]) * sc);
+              pk.w = pack2<BF16>(__uint_as_float(r[8 * v4 + 6]) * sc, __uint_as_float(r[8 * v4 + 7]) * sc);
+              dst[v4] = pk;
+            }
           }
         }
       }
@@ -406,7 +441,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncwarp();
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == L::WARP_MMA) {
     tc_fence_after();
     tmem_dealloc(tmem, L::TM_COLS);
   }
@@ -420,6 +455,9 @@ struct BwdBLayout {
   static constexpr bool TRANS = (D == 128);      // accumulate dV^T / dK^T (M = D)
   static constexpr int KB = TRANS ? 64 : 128;    // keys per CTA
   static constexpr int NS = TRANS ? 2 : 1;       // S / dS TMEM buffers
+  static constexpr int NWG = NS;                 // softmax warpgroups; WG w takes iterations it % NWG == w
+  static constexpr int THREADS = 128 * NWG + 64; // + TMA warp + MMA warp
+  static constexpr int WARP_TMA = 4 * NWG, WARP_MMA = 4 * NWG + 1;
   static constexpr int QS = 2, PS = 2;           // Q/dO and P/dP shared-memory stages
   static constexpr int QBOX = 128 * 128;         // [128 rows][64 cols] box
   static constexpr int KBOX = KB * 128;          // [KB rows][64 cols] box
@@ -455,7 +493,7 @@ __device__ __forceinline__ void decode_block(int L, int n_heads, int n_blocks, i
 }
 
 template <int D, bool BF16>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
     coalibi_bwd_b_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
                          const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                          const BwdParams p) {
@@ -511,7 +549,7 @@ __global__ void __launch_bounds__(192, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == L::WARP_MMA) {
     tmem_alloc(tmem_slot, L::TM_COLS);
     tmem_relinquish();
   }
@@ -520,7 +558,7 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == L::WARP_TMA) {
     if (lane == 0 && NIT > 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmDO);
@@ -554,7 +592,7 @@ __global__ void __launch_bounds__(192, 1)
         if (uses > 0) mbar_drain(&qdo_full[s], (uses - 1) & 1, g.timeout_ns);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == L::WARP_MMA) {
     if (lane == 0 && NIT > 0) {
       constexpr uint32_t idS = make_idesc_f16(BF16, 128, KB, false, false);
       // TRANS: dV^T[d][key] = dO^T[d][row] P[row][key]  (A = dO^T MN-major, B = P MN-major), M = D, N = KB
@@ -626,13 +664,14 @@ __global__ void __launch_bounds__(192, 1)
       mbar_drain(mma_idle, 0, g.timeout_ns);
     }
   } else {
-    const int t_row = threadIdx.x;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const int wg = warp >> 2;
+    const int t_row = threadIdx.x & 127;
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const float c_sig = -p.sm_scale * kLog2e;
     const float c_a = p.sm_scale * kLog2e;
     const int kb64 = key0 / 64;
     bool ok = true;
-    for (int it = 0; it < NIT; ++it) {
+    for (int it = wg; it < NIT; it += L::NWG) {
       const int hh = gkv * G + it / nM;
       const int m = m_start + it % nM;
       const int bhq = b * p.Hq + hh;
@@ -693,9 +732,10 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       mbar_arrive(&pp_full[ps]);
     }
-    // epilogue
+    // epilogue (warpgroup 0 covers all 128 TMEM lanes)
     const int bkv = hk;
-    if (NIT > 0) {
+    if (wg != 0) {
+    } else if (NIT > 0) {
       if (ok) {
         ok = mbar_wait(acc_done, 0, g);
         ok = __all_sync(0xffffffffu, ok);
@@ -785,7 +825,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncwarp();
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == L::WARP_MMA) {
     tc_fence_after();
     tmem_dealloc(tmem, L::TM_COLS);
   }
@@ -850,6 +890,9 @@ inline int bwd_launch_t(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigne
   if ((rc = make_tmap(&tdo, a.dout, D, a.Sq, a.B * a.Hq, 128, BF16))) return rc;
   if ((rc = make_tmap(&tk, a.k, D, a.Skv, a.B * a.Hkv, 128, BF16))) return rc;
   if ((rc = make_tmap(&tv, a.v, D, a.Skv, a.B * a.Hkv, 128, BF16))) return rc;
+  CUtensorMap tka, tva;
+  if ((rc = make_tmap(&tka, a.k, D, a.Skv, a.B * a.Hkv, BwdALayout<D>::BN, BF16))) return rc;
+  if ((rc = make_tmap(&tva, a.v, D, a.Skv, a.B * a.Hkv, BwdALayout<D>::BN, BF16))) return rc;
   if ((rc = make_tmap(&tkb, a.k, D, a.Skv, a.B * a.Hkv, BwdBLayout<D>::KB, BF16))) return rc;
   if ((rc = make_tmap(&tvb, a.v, D, a.Skv, a.B * a.Hkv, BwdBLayout<D>::KB, BF16))) return rc;
 
@@ -857,9 +900,11 @@ inline int bwd_launch_t(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigne
   if (phases & 1)
     coalibi_bwd_delta_kernel<D, BF16><<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(p);
   if (phases & 2)
-    coalibi_bwd_a_kernel<D, BF16><<<a.B * a.Hq * p.n_qtiles, 192, BwdALayout<D>::ALLOC, stream>>>(tq, tdo, tk, tv, p);
+    coalibi_bwd_a_kernel<D, BF16><<<a.B * a.Hq * ((p.n_qtiles + 1) / 2), BwdALayout<D>::THREADS,
+                                    BwdALayout<D>::ALLOC, stream>>>(tq, tdo, tka, tva, p);
   if (phases & 4)
-    coalibi_bwd_b_kernel<D, BF16><<<a.B * a.Hkv * p.n_blocks, 192, BwdBLayout<D>::ALLOC, stream>>>(tq, tdo, tkb, tvb, p);
+    coalibi_bwd_b_kernel<D, BF16>
+        <<<a.B * a.Hkv * p.n_blocks, BwdBLayout<D>::THREADS, BwdBLayout<D>::ALLOC, stream>>>(tq, tdo, tkb, tvb, p);
   return cudaGetLastError() == cudaSuccess ? COALIBI_OK : COALIBI_ERR_LAUNCH;
 }
 

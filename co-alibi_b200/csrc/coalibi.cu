@@ -145,8 +145,8 @@ unsigned long long timeout_ns(unsigned ms) {
 template <int D, bool BF16>
 int launch_fwd_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const FwdParams& p,
                cudaStream_t stream) {
-  const int grid = p.B * p.Hq * p.n_qtiles;
-  coalibi_fwd_kernel<D, BF16><<<grid, 192, FwdLayout<D>::ALLOC, stream>>>(tq, tk, tv, p);
+  const int grid = p.B * p.Hq * ((p.n_qtiles + 1) / 2);
+  coalibi_fwd_kernel<D, BF16><<<grid, FwdLayout<D>::THREADS, FwdLayout<D>::ALLOC, stream>>>(tq, tk, tv, p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     snprintf(g_last_error, sizeof(g_last_error), "forward launch: %s", cudaGetErrorString(e));

@@ -67,6 +67,8 @@ __device__ __forceinline__ void decode_tile(int L, int BH, int nQ, int& bh, int&
   m = nQ - 1 - mq;
 }
 
+// Two 128-row query tiles ("slots") per CTA, ping-ponging on two softmax
+// warpgroups so that one slot's exponentials overlap the other's MMAs.
 template <int D>
 struct FwdLayout {
   static constexpr int BM = 128, BN = 128;
@@ -75,18 +77,25 @@ struct FwdLayout {
   static constexpr int BOX = 128 * 128;  // one [128 rows][64 cols] 16-bit box, SW128
   static constexpr int TILE = BN * D * 2;
   static constexpr int QB = BM * D * 2;
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = OFF_Q + QB;
+  static constexpr int OFF_Q = 0;  // two query tiles
+  static constexpr int OFF_K = OFF_Q + 2 * QB;
   static constexpr int OFF_V = OFF_K + KS * TILE;
   static constexpr int OFF_BAR = OFF_V + VS * TILE;
-  static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 2 + 2 + 1 + 1;
+  static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 2 + 2 + 2 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 16;
   static constexpr int ALLOC = BYTES + 1024;
-  static constexpr uint32_t TM_S = 0;
-  static constexpr uint32_t TM_O = 256;
-  static constexpr uint32_t TM_P = 256 + D;
+  // warpgroups 0, 1: softmax of slot 0 / 1; warpgroup 2: TMA warp, MMA warp, two idle warps.
+  // Launched at 168 registers/thread (3 warps per SM sub-partition); the softmax
+  // warpgroups then take 232 and the producer warpgroup keeps 40: 2*232 + 40 = 3*168.
+  static constexpr int THREADS = 384;
+  static constexpr int REGS_SOFTMAX = 216, REGS_PRODUCER = 72;
+  static_assert(2 * REGS_SOFTMAX + REGS_PRODUCER <= 3 * 168, "register split exceeds the launch allocation");
+  // TMEM per slot s at column 256*s: S [0,128) with P aliased in [0,64); O [128,128+D)
+  static constexpr uint32_t TM_SLOT = 256;
+  static constexpr uint32_t TM_O = 128;
   static constexpr uint32_t TM_COLS = 512;
+  static_assert(ALLOC <= 232448, "shared memory budget");
 };
 
 // Reverse scan of one 128-key score row (raw q.k dot products in sreg[]):
@@ -114,7 +123,7 @@ __device__ __forceinline__ float fwd_scan_tile(uint32_t* sreg, float& run, int k
 }
 
 template <int D, bool BF16>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(384, 1)
     coalibi_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
   using L = FwdLayout<D>;
@@ -130,25 +139,30 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* k_empty = k_full + L::KS;
   uint64_t* v_full = k_empty + L::KS;
   uint64_t* v_empty = v_full + L::VS;
-  uint64_t* s_full = v_empty + L::VS;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* pv_done = p_full + 2;
-  uint64_t* mma_idle = pv_done + 1;
+  uint64_t* s_full = v_empty + L::VS;  // [2] per slot
+  uint64_t* p_full = s_full + 2;       // [2]
+  uint64_t* pv_done = p_full + 2;      // [2]
+  uint64_t* mma_idle = pv_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
   const int warp = warp_id();
   const int lane = lane_id();
   const int BH = p.B * p.Hq;
-  int bh, m;
-  decode_tile(blockIdx.x, BH, p.n_qtiles, bh, m);
+  const int n_pairs = (p.n_qtiles + 1) / 2;
+  int bh, pair;
+  decode_tile(blockIdx.x, BH, n_pairs, bh, pair);
   const int b = bh / p.Hq;
   const int h = bh - b * p.Hq;
-  const int kvh = h / (p.Hq / p.Hkv);
-  const int zkv = b * p.Hkv + kvh;
-  // visited key tiles: 0..last (causal: tiles starting at or before the tile's last row)
-  const int last = p.causal ? min(p.n_kvtiles - 1, (m * L::BM + L::BM - 1) / L::BN) : p.n_kvtiles - 1;
-  const int N = last + 1;
+  const int zkv = b * p.Hkv + h / (p.Hq / p.Hkv);
+  const bool has1 = (2 * pair + 1) < p.n_qtiles;
+  // last key tile visited by each slot (causal: tiles starting at or before the slot's last row)
+  const int last0 = p.causal ? min(p.n_kvtiles - 1, 2 * pair) : p.n_kvtiles - 1;
+  const int last1 = has1 ? (p.causal ? min(p.n_kvtiles - 1, 2 * pair + 1) : p.n_kvtiles - 1) : -1;
+  const int last = max(last0, last1);
+  const int N = last + 1;  // tile n of the sweep is key tile last - n
+  // slot s is active on sweep step n iff its query tile sees key tile last - n
+  auto active = [&](int s, int n) -> bool { return (last - n) <= (s == 0 ? last0 : last1); };
 
   CtaGuard g{abort_flag, p.status, p.timeout_ns};
 
@@ -165,13 +179,13 @@ __global__ void __launch_bounds__(192, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
+      mbar_init(&pv_done[i], 1);
     }
-    mbar_init(pv_done, 1);
     mbar_init(mma_idle, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, L::TM_COLS);
     tmem_relinquish();
   }
@@ -180,15 +194,19 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp >= 8) {
+    regs_decrease<L::REGS_PRODUCER>();
+  if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(q_full, L::QB);
+      mbar_arrive_expect_tx(q_full, (has1 ? 2 : 1) * L::QB);
+      for (int s = 0; s < (has1 ? 2 : 1); ++s)
 #pragma unroll
-      for (int bx = 0; bx < D / 64; ++bx) tma_load_3d(sQ + bx * L::BOX, &tmQ, q_full, bx * 64, m * L::BM, bh);
+        for (int bx = 0; bx < D / 64; ++bx)
+          tma_load_3d(sQ + s * L::QB + bx * L::BOX, &tmQ, q_full, bx * 64, (2 * pair + s) * L::BM, bh);
       int nk = 0, nv = 0;
       for (int n = 0; n < N; ++n) {
         const int key0 = (last - n) * L::BN;
@@ -218,7 +236,7 @@ __global__ void __launch_bounds__(192, 1)
         if (uses > 0) mbar_drain(&v_full[s], (uses - 1) & 1, g.timeout_ns);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idS = make_idesc_f16(BF16, 128, L::BN, false, false);
@@ -226,52 +244,88 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t q_addr = smem_u32(sQ);
       const uint32_t k_addr = smem_u32(sK);
       const uint32_t v_addr = smem_u32(sV);
-      auto issue_S = [&](int n) -> bool {
-        const int ks = n % L::KS;
-        if (!mbar_wait(&k_full[ks], (n / L::KS) & 1, g)) return false;
+      // Slots are served in strict alternation: PV_0(n), S_0(n+1), PV_1(n), S_1(n+1), ...
+      // This keeps the two softmax warpgroups half a tile apart (ping-pong): while
+      // one waits for its MMAs the other has the exponential unit to itself.
+      int k_waited = -1, v_waited = -1;
+      int pv_cnt[2] = {0, 0};  // PVs issued per slot
+      int k_uses[L::KS] = {}, v_uses[L::VS] = {};
+      auto n_active = [&](int n) { return (active(0, n) ? 1 : 0) + (active(1, n) ? 1 : 0); };
+      auto wait_k = [&](int n) -> bool {
+        for (; k_waited < n; ++k_waited)
+          if (!mbar_wait(&k_full[(k_waited + 1) % L::KS], ((k_waited + 1) / L::KS) & 1, g)) return false;
+        return true;
+      };
+      auto wait_v = [&](int n) -> bool {
+        for (; v_waited < n; ++v_waited)
+          if (!mbar_wait(&v_full[(v_waited + 1) % L::VS], ((v_waited + 1) / L::VS) & 1, g)) return false;
+        return true;
+      };
+      auto issue_S = [&](int s, int n) -> bool {
+        if (!wait_k(n)) return false;
         tc_fence_after();
-        const uint32_t d = tmem + L::TM_S + (n & 1) * 128;
+        const int ks = n % L::KS;
+        const uint32_t d = tmem + s * L::TM_SLOT;
+        const uint32_t qa = q_addr + s * L::QB;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * L::BOX + (kk & 3) * 32;
-          umma_ss(d, make_sdesc_sw128(q_addr + off, 16, 1024),
-                  make_sdesc_sw128(k_addr + ks * L::TILE + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
+          umma_ss(d, make_sdesc_sw128(qa + off, 16, 1024), make_sdesc_sw128(k_addr + ks * L::TILE + off, 16, 1024),
+                  idS, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&k_empty[ks]);
-        umma_commit(&s_full[n & 1]);
-        return true;
-      };
-      auto issue_PV = [&](int n) -> bool {
-        if (!mbar_wait(&p_full[n & 1], (n >> 1) & 1, g)) return false;
-        const int vs = n % L::VS;
-        if (!mbar_wait(&v_full[vs], (n / L::VS) & 1, g)) return false;
-        tc_fence_after();
-        const uint32_t pa = tmem + L::TM_P + (n & 1) * 64;
-#pragma unroll
-        for (int kk = 0; kk < L::BN / 16; ++kk) {
-          const uint64_t vdesc = make_sdesc_sw128(v_addr + vs * L::TILE + kk * 16 * 128, L::BOX, 1024);
-          umma_ts(tmem + L::TM_O, pa + kk * 8, vdesc, idPV, (n > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&s_full[s]);
+        if (++k_uses[ks] == n_active(n)) {  // every active slot has read K(n): release the stage
+          k_uses[ks] = 0;
+          umma_commit(&k_empty[ks]);
         }
-        umma_commit(&v_empty[vs]);
-        umma_commit(pv_done);
         return true;
       };
       bool ok = mbar_wait(q_full, 0, g);
-      if (ok) ok = issue_S(0);
-      if (ok && N > 1) ok = issue_S(1);
+      for (int s = 0; ok && s < 2; ++s)
+        if (active(s, 0)) ok = issue_S(s, 0);
       for (int n = 0; ok && n < N; ++n) {
-        ok = issue_PV(n);
-        if (ok && n + 2 < N) ok = issue_S(n + 2);
+        for (int s = 0; ok && s < 2; ++s) {
+          const bool act = active(s, n);
+          if (act) {
+            // P_s(n) published by the slot's softmax warps
+            if (!(ok = mbar_wait(&p_full[s], pv_cnt[s] & 1, g))) break;
+            if (!(ok = wait_v(n))) break;
+            tc_fence_after();
+            const int vs = n % L::VS;
+            const uint32_t pa = tmem + s * L::TM_SLOT;
+#pragma unroll
+            for (int kk = 0; kk < L::BN / 16; ++kk) {
+              const uint64_t vdesc = make_sdesc_sw128(v_addr + vs * L::TILE + kk * 16 * 128, L::BOX, 1024);
+              umma_ts(tmem + s * L::TM_SLOT + L::TM_O, pa + kk * 8, vdesc, idPV,
+                      (pv_cnt[s] > 0 || kk > 0) ? 1u : 0u);
+            }
+            umma_commit(&pv_done[s]);
+            ++pv_cnt[s];
+            if (++v_uses[vs] == n_active(n)) {
+              v_uses[vs] = 0;
+              umma_commit(&v_empty[vs]);
+            }
+          }
+          if (n + 1 < N && active(s, n + 1)) {
+            // S_s(n+1) overwrites the columns P_s(n) is read from: wait for PV_s(n)
+            if (act && !(ok = mbar_wait(&pv_done[s], (pv_cnt[s] - 1) & 1, g))) break;
+            ok = issue_S(s, n + 1);
+          }
+        }
       }
       // every MMA issued above must have finished before TMEM is released
       umma_commit(mma_idle);
       mbar_drain(mma_idle, 0, g.timeout_ns);
     }
+  }
   } else {
-    // ------------------------------------------------------------ softmax warps 0-3
-    const int t = threadIdx.x;  // row within the tile
-    const int row = m * L::BM + t;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    regs_increase<L::REGS_SOFTMAX>();
+    // ------------------------------------------------------------ softmax warpgroups 0 and 1
+    const int slot = warp >> 2;
+    const int t = threadIdx.x & 127;  // row within the slot's tile
+    const int qt = 2 * pair + slot;
+    const int row = qt * L::BM + t;
+    const uint32_t lane_base = tmem + slot * L::TM_SLOT + ((uint32_t)((warp & 3) * 32) << 16);
     const float slope = load_slope(p.slopes, p.slopes_dtype, h);
     const float c_sig = -p.sm_scale * kLog2e;
     const float c_a = p.sm_scale * kLog2e;
@@ -279,102 +333,101 @@ __global__ void __launch_bounds__(192, 1)
     const int lim = p.causal ? min(row + 1, p.Skv) : p.Skv;
     float m_ref = -INFINITY, l = 0.f, run = 0.f;
     bool ok = true;
-    for (int n = 0; n < N; ++n) {
-      const int key0 = (last - n) * L::BN;
-      ok = mbar_wait(&s_full[n & 1], (n >> 1) & 1, g);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      tc_fence_after();
-      uint32_t sreg[128];
-      const uint32_t sa = lane_base + L::TM_S + (n & 1) * 128;
-      tmem_ld32(sa, sreg);
-      tmem_ld32(sa + 32, sreg + 32);
-      tmem_ld32(sa + 64, sreg + 64);
-      tmem_ld32(sa + 96, sreg + 96);
-      tmem_ld_wait32(sreg);
-      tmem_ld_fence32(sreg + 32);
-      tmem_ld_fence32(sreg + 64);
-      tmem_ld_fence32(sreg + 96);
-
-      const bool masked = (key0 + L::BN > p.Skv) || (p.causal && key0 + L::BN - 1 > m * L::BM);
-      const float tmax = masked ? fwd_scan_tile<true>(sreg, run, key0, lim, c_sig, c_a, slope2)
-                                : fwd_scan_tile<false>(sreg, run, key0, lim, c_sig, c_a, slope2);
-      float alpha = 1.f;
-      bool resc = false;
-      if (m_ref == -INFINITY) {
-        m_ref = tmax;
-      } else if (tmax > m_ref + 8.f) {
-        alpha = ex2_approx(m_ref - tmax);
-        m_ref = tmax;
-        resc = true;
-      }
-      const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-      uint32_t preg[64];
-      float ls0 = 0.f, ls1 = 0.f;
-#pragma unroll
-      for (int j = 0; j < 64; ++j) {
-        const float e0 = ex2_approx(__uint_as_float(sreg[2 * j]) - m_use);
-        const float e1 = ex2_approx(__uint_as_float(sreg[2 * j + 1]) - m_use);
-        ls0 += e0;
-        ls1 += e1;
-        preg[j] = pack2<BF16>(e0, e1);
-      }
-      l = fmaf(l, alpha, ls0 + ls1);
-
-      if (n > 0) {
-        // O (and the P buffer written next) must be free of PV_{n-1}
-        ok = mbar_wait(pv_done, (n - 1) & 1, g);
+    int it = 0;
+    if (slot == 0 || has1) {
+      for (int n = 0; n < N; ++n) {
+        if (!active(slot, n)) continue;
+        const int key0 = (last - n) * L::BN;
+        ok = mbar_wait(&s_full[slot], it & 1, g);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
+        uint32_t sreg[128];
+        tmem_ld32(lane_base, sreg);
+        tmem_ld32(lane_base + 32, sreg + 32);
+        tmem_ld32(lane_base + 64, sreg + 64);
+        tmem_ld32(lane_base + 96, sreg + 96);
+        tmem_ld_wait32(sreg);
+        tmem_ld_fence32(sreg + 32);
+        tmem_ld_fence32(sreg + 64);
+        tmem_ld_fence32(sreg + 96);
+
+        const bool masked = (key0 + L::BN > p.Skv) || (p.causal && key0 + L::BN - 1 > qt * L::BM);
+        const float tmax = masked ? fwd_scan_tile<true>(sreg, run, key0, lim, c_sig, c_a, slope2)
+                                  : fwd_scan_tile<false>(sreg, run, key0, lim, c_sig, c_a, slope2);
+        float alpha = 1.f;
+        bool resc = false;
+        if (m_ref == -INFINITY) {
+          m_ref = tmax;
+        } else if (tmax > m_ref + 8.f) {
+          alpha = ex2_approx(m_ref - tmax);
+          m_ref = tmax;
+          resc = true;
+        }
+        const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
+        // O is free of this slot's previous PV: S_s(it) was issued only after it completed.
+        if (__any_sync(0xffffffffu, resc)) {
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t oreg[32];
+            tmem_ld32(lane_base + L::TM_O + c * 32, oreg);
+            tmem_ld_wait32(oreg);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) oreg[j] = __float_as_uint(__uint_as_float(oreg[j]) * alpha);
+            tmem_st32(lane_base + L::TM_O + c * 32, oreg);
+          }
+        }
+        float ls0 = 0.f, ls1 = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t preg[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float e0 = ex2_approx(__uint_as_float(sreg[32 * c + 2 * j]) - m_use);
+            const float e1 = ex2_approx(__uint_as_float(sreg[32 * c + 2 * j + 1]) - m_use);
+            ls0 += e0;
+            ls1 += e1;
+            preg[j] = pack2<BF16>(e0, e1);
+          }
+          tmem_st16(lane_base + c * 16, preg);  // P aliased over the S columns already read
+        }
+        l = fmaf(l, alpha, ls0 + ls1);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&p_full[slot]);
+        ++it;
       }
-      if (__any_sync(0xffffffffu, resc)) {
+      if (ok && it > 0) {
+        ok = mbar_wait(&pv_done[slot], (it - 1) & 1, g);
+        ok = __all_sync(0xffffffffu, ok);
+      }
+      if (ok && it > 0) {
+        tc_fence_after();
+        const float inv = 1.0f / (l + 1e-9f);
+        uint8_t* orow = static_cast<uint8_t*>(p.o) + ((size_t)bh * p.Sq + row) * D * 2;
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t oreg[32];
           tmem_ld32(lane_base + L::TM_O + c * 32, oreg);
           tmem_ld_wait32(oreg);
+          if (row < p.Sq) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) oreg[j] = __float_as_uint(__uint_as_float(oreg[j]) * alpha);
-          tmem_st32(lane_base + L::TM_O + c * 32, oreg);
-        }
-      }
-      tmem_st32(lane_base + L::TM_P + (n & 1) * 64, preg);
-      tmem_st32(lane_base + L::TM_P + (n & 1) * 64 + 32, preg + 32);
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&p_full[n & 1]);
-    }
-    if (ok) {
-      ok = mbar_wait(pv_done, (N - 1) & 1, g);
-      ok = __all_sync(0xffffffffu, ok);
-    }
-    if (ok) {
-      tc_fence_after();
-      const float inv = 1.0f / (l + 1e-9f);
-      uint8_t* orow = static_cast<uint8_t*>(p.o) + ((size_t)bh * p.Sq + row) * D * 2;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t oreg[32];
-        tmem_ld32(lane_base + L::TM_O + c * 32, oreg);
-        tmem_ld_wait32(oreg);
-        if (row < p.Sq) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
-#pragma unroll
-          for (int v4 = 0; v4 < 4; ++v4) {
-            uint4 pk;
-            pk.x = pack2<BF16>(__uint_as_float(oreg[8 * v4 + 0]) * inv, __uint_as_float(oreg[8 * v4 + 1]) * inv);
-            pk.y = pack2<BF16>(__uint_as_float(oreg[8 * v4 + 2]) * inv, __uint_as_float(oreg[8 * v4 + 3]) * inv);
-            pk.z = pack2<BF16>(__uint_as_float(oreg[8 * v4 + 4]) * inv, __uint_as_float(oreg[8 * v4 + 5]) * inv);
-            pk.w = pack2<BF16>(__uint_as_float(oreg[8 * v4 + 6]) * inv, __uint_as_float(oreg[8 * v4 + 7]) * inv);
-            dst[v4] = pk;
+            for (int v4 = 0; v4 < 4; ++v4) {
+              uint4 pk;
+              pk.x = pack2<BF16>(__uint_as_float(oreg[8 * v4 + 0]) * inv, __uint_as_float(oreg[8 * v4 + 1]) * inv);
+              pk.y = pack2<BF16>(__uint_as_float(oreg[8 * v4 + 2]) * inv, __uint_as_float(oreg[8 * v4 + 3]) * inv);
+              pk.z = pack2<BF16>(__uint_as_float(oreg[8 * v4 + 4]) * inv, __uint_as_float(oreg[8 * v4 + 5]) * inv);
+              pk.w = pack2<BF16>(__uint_as_float(oreg[8 * v4 + 6]) * inv, __uint_as_float(oreg[8 * v4 + 7]) * inv);
+              dst[v4] = pk;
+            }
           }
         }
-      }
-      if (row < p.Sq) {
-        const size_t ri = (size_t)bh * p.Sq + row;
-        p.lse[ri] = m_ref * kLn2 + logf(l + 1e-9f);
-        p.rowsig[ri] = run;
+        if (row < p.Sq) {
+          const size_t ri = (size_t)bh * p.Sq + row;
+          p.lse[ri] = m_ref * kLn2 + logf(l + 1e-9f);
+          p.rowsig[ri] = run;
+        }
       }
     }
   }
@@ -382,7 +435,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncwarp();
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, L::TM_COLS);
   }

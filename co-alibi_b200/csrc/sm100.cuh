@@ -77,6 +77,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe (test_wait never suspends the thread, unlike try_wait).
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait until the phase with the given parity has completed.  Returns false
 // (and raises the CTA abort flag) when the wait exceeds the guard's timeout or
 // another role of the CTA has already aborted.
@@ -271,6 +284,19 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ----------------------------------------------------------------------------
+// Per-warpgroup register re-balancing (all 4 warps of a warpgroup execute it).
+// The increases of all warpgroups must fit in what the CTA was launched with.
+// ----------------------------------------------------------------------------
+template <int N>
+__device__ __forceinline__ void regs_increase() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_decrease() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// ----------------------------------------------------------------------------
 // Scalar helpers
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -284,7 +310,7 @@ __device__ __forceinline__ float rcp_approx(float x) {
   return y;
 }
 
-// sigmoid(x) with x pre-multiplied by -log2(e): 1 / (1 + 2^(-x*log2 e))
+// sigmoid(p) = 1 / (1 + 2^xn) with xn = -p*log2(e): MUFU ex2 + MUFU rcp.
 __device__ __forceinline__ float sigmoid_from_neg_log2(float xn) { return rcp_approx(1.0f + ex2_approx(xn)); }
 
 template <bool BF16>

@@ -69,7 +69,8 @@ def test_forward_side_outputs(api, case):
     torch.cuda.synchronize()
     _, lse_ref, rs_ref = oracle_fwd(q, k, v, causal, scale)
     assert (lse.cpu().double() - lse_ref).abs().max().item() < 2e-3
-    assert ((rowsig.cpu().double() - rs_ref).abs() / rs_ref.abs().clamp_min(1.0)).max().item() < 1e-4
+    # rowsig = sum_j sigmoid(p_ij): pins the sigmoid's accuracy (float32 sums of ~S terms)
+    assert ((rowsig.cpu().double() - rs_ref).abs() / rs_ref.abs().clamp_min(1.0)).max().item() < 2e-5
 
 
 @pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLD, "case_*.npz"))),
