@@ -346,8 +346,8 @@ __global__ void __launch_bounds__(320, 1)
             ++dq_cnt[s];
           }
           if (n + 1 < N && active(s, n + 1)) {
-            // S_s(n+1) overwrites the columns dP_s(n) is read from
-            if (act && !(ok = mbar_wait(&dq_done[s], (dq_cnt[s] - 1) & 1, g))) break;
+            // S_s(n+1) overwrites the TMEM columns dP_s(n) is read from; tcgen05.mma
+            // ops issued by one thread execute in order, so no wait is needed.
             ok = issue_SdS(s, n + 1);
           }
         }
@@ -601,9 +601,8 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
                                           : make_idesc_f16(BF16, KB, D, true, true);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
       const uint32_t qdo_addr = smem_u32(sQDO), p_addr = smem_u32(sP);
-      auto issue_SdS = [&](int it) -> bool {
+      auto issue_SdS = [&](int it) {
         const int st = it % L::QS;
-        if (!mbar_wait(&qdo_full[st], (it / L::QS) & 1, g)) return false;
         tc_fence_after();
         const uint32_t qa = qdo_addr + st * 2 * L::QB, da = qa + L::QB;
         const int sb = it % L::NS;
@@ -622,42 +621,79 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
                   make_sdesc_sw128(v_addr + ko, 16, 1024), idS, kk > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[sb]);
-        return true;
       };
+      // Non-blocking issue loop: dV/dK(it) go out as soon as P/dP(it) are
+      // published -- never queued behind the load of a later query tile -- which
+      // frees that tile's Q/dO stage for the next load as early as possible;
+      // S/dS(j) go out once Q/dO(j) landed and their TMEM buffer is free.
       bool ok = mbar_wait(kv_full, 0, g);
-      if (ok) ok = issue_SdS(0);
-      for (int it = 0; ok && it < NIT; ++it) {
-        if (it + 1 < NIT) {
-          if (L::NS == 1) ok = mbar_wait(s_free, it & 1, g);
-          if (ok) ok = issue_SdS(it + 1);
-        }
-        const int ps = it % L::PS;
-        if (ok) ok = mbar_wait(&pp_full[ps], (it / L::PS) & 1, g);
-        if (!ok) break;
-        tc_fence_after();
-        const int st = it % L::QS;
-        const uint32_t qa = qdo_addr + st * 2 * L::QB, da = qa + L::QB;
-        const uint32_t pa = p_addr + ps * 2 * L::PB, dpa = pa + L::PB;
-        const uint32_t acc = (it > 0) ? 1u : 0u;
+      int next_s = 0, next_d = 0, sfree_seen = 0;
+      int idle = 0;
+      uint64_t t_idle = 0;
+      while (ok && next_d < NIT) {
+        bool progressed = false;
+        if (next_d < next_s && mbar_test(&pp_full[next_d % L::PS], (next_d / L::PS) & 1)) {
+          const int it = next_d;
+          tc_fence_after();
+          const int ps = it % L::PS;
+          const int st = it % L::QS;
+          const uint32_t qa = qdo_addr + st * 2 * L::QB, da = qa + L::QB;
+          const uint32_t pa = p_addr + ps * 2 * L::PB, dpa = pa + L::PB;
+          const uint32_t acc = (it > 0) ? 1u : 0u;
 #pragma unroll
-        for (int kk = 0; kk < 128 / 16; ++kk) {  // K = 128 query rows, 16 per MMA
-          const uint32_t ko = kk * 16 * 128;        // 16 rows of 128 bytes
-          if (L::TRANS) {
-            // A: dO^T / Q^T (MN = d, 64-wide blocks one box apart), B: P / dP (MN = keys, one block)
-            umma_ss(tmem + L::TM_DV, make_sdesc_sw128(da + ko, L::QBOX, 1024),
-                    make_sdesc_sw128(pa + ko, L::PB, 1024), idAcc, (acc || kk > 0) ? 1u : 0u);
-            umma_ss(tmem + L::TM_DK, make_sdesc_sw128(qa + ko, L::QBOX, 1024),
-                    make_sdesc_sw128(dpa + ko, L::PB, 1024), idAcc, (acc || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < 128 / 16; ++kk) {  // K = 128 query rows, 16 per MMA
+            const uint32_t ko = kk * 16 * 128;        // 16 rows of 128 bytes
+            if (L::TRANS) {
+              // A: dO^T / Q^T (MN = d, 64-wide blocks one box apart), B: P / dP (MN = keys, one block)
+              umma_ss(tmem + L::TM_DV, make_sdesc_sw128(da + ko, L::QBOX, 1024),
+                      make_sdesc_sw128(pa + ko, L::PB, 1024), idAcc, (acc || kk > 0) ? 1u : 0u);
+              umma_ss(tmem + L::TM_DK, make_sdesc_sw128(qa + ko, L::QBOX, 1024),
+                      make_sdesc_sw128(dpa + ko, L::PB, 1024), idAcc, (acc || kk > 0) ? 1u : 0u);
+            } else {
+              // A: P^T / dP^T (MN = keys, two 64-key blocks 128*128 bytes apart), B: dO / Q (MN = d)
+              umma_ss(tmem + L::TM_DV, make_sdesc_sw128(pa + ko, 128 * 128, 1024),
+                      make_sdesc_sw128(da + ko, L::QBOX, 1024), idAcc, (acc || kk > 0) ? 1u : 0u);
+              umma_ss(tmem + L::TM_DK, make_sdesc_sw128(dpa + ko, 128 * 128, 1024),
+                      make_sdesc_sw128(qa + ko, L::QBOX, 1024), idAcc, (acc || kk > 0) ? 1u : 0u);
+            }
+          }
+          umma_commit(&pp_empty[ps]);
+          umma_commit(&qdo_empty[st]);
+          ++next_d;
+          progressed = true;
+        }
+        if (next_s < NIT) {
+          // TMEM buffer of S/dS(next_s): with two buffers, free once P/dP(next_s - 2) was
+          // published (the softmax read S/dS before that); with one, once s_free says so.
+          bool buf_free;
+          if (L::NS == 2) {
+            buf_free = next_s < next_d + 2;
           } else {
-            // A: P^T / dP^T (MN = keys, two 64-key blocks 128*128 bytes apart), B: dO / Q (MN = d)
-            umma_ss(tmem + L::TM_DV, make_sdesc_sw128(pa + ko, 128 * 128, 1024),
-                    make_sdesc_sw128(da + ko, L::QBOX, 1024), idAcc, (acc || kk > 0) ? 1u : 0u);
-            umma_ss(tmem + L::TM_DK, make_sdesc_sw128(dpa + ko, 128 * 128, 1024),
-                    make_sdesc_sw128(qa + ko, L::QBOX, 1024), idAcc, (acc || kk > 0) ? 1u : 0u);
+            if (sfree_seen < next_s && mbar_test(s_free, sfree_seen & 1)) ++sfree_seen;
+            buf_free = sfree_seen >= next_s;
+          }
+          if (buf_free && mbar_test(&qdo_full[next_s % L::QS], (next_s / L::QS) & 1)) {
+            issue_SdS(next_s);
+            ++next_s;
+            progressed = true;
           }
         }
-        umma_commit(&pp_empty[ps]);
-        umma_commit(&qdo_empty[st]);
+        if (progressed) {
+          idle = 0;
+          t_idle = 0;
+        } else {
+          __nanosleep(32);
+          if (++idle == 64) {
+            idle = 0;
+            const uint64_t now = global_timer_ns();
+            if (t_idle == 0) t_idle = now;
+            if (g.aborted()) ok = false;
+            else if (now - t_idle > g.timeout_ns) {
+              g.raise(kStatusTimeout);
+              ok = false;
+            }
+          }
+        }
       }
       if (ok) umma_commit(acc_done);
       umma_commit(mma_idle);
@@ -671,19 +707,39 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
     const float c_a = p.sm_scale * kLog2e;
     const int kb64 = key0 / 64;
     bool ok = true;
+    // Per-row inputs of an iteration (lse, delta, and pass A's carries at this key
+    // block) are loaded one iteration ahead so their latency overlaps the current
+    // iteration's work instead of stalling its start.
+    struct RowIn {
+      float lse2, delta, zs, cacc;
+    };
+    auto load_row = [&](int it_) -> RowIn {
+      RowIn r{0.f, 0.f, 0.f, 0.f};
+      if (it_ >= NIT) return r;
+      const int hh_ = gkv * G + it_ / nM;
+      const int m_ = m_start + it_ % nM;
+      const int bhq_ = b * p.Hq + hh_;
+      const int row_ = m_ * 128 + t_row;
+      if (row_ < p.Sq) r.lse2 = p.lse[(size_t)bhq_ * p.Sq + row_] * kLog2e;
+      r.delta = p.delta[(size_t)bhq_ * p.sq_pad + row_];
+      const float2 cin = p.carry[((size_t)bhq_ * p.n_kb64 + kb64) * p.sq_pad + row_];
+      r.zs = cin.x;
+      r.cacc = cin.y;
+      return r;
+    };
+    RowIn nxt = load_row(wg);
     for (int it = wg; it < NIT; it += L::NWG) {
       const int hh = gkv * G + it / nM;
       const int m = m_start + it % nM;
-      const int bhq = b * p.Hq + hh;
       const int row = m * 128 + t_row;
       const bool row_ok = row < p.Sq;
       const float slope = load_slope(p.slopes, p.slopes_dtype, hh);
       const float slope2 = slope * kLog2e;
-      const size_t ri = (size_t)bhq * p.Sq + row;
-      const float lse2 = row_ok ? p.lse[ri] * kLog2e : 0.f;
-      const float delta = p.delta[(size_t)bhq * p.sq_pad + row];
-      const float2 cin = p.carry[((size_t)bhq * p.n_kb64 + kb64) * p.sq_pad + row];
-      float zs = cin.x, cacc = cin.y;
+      const RowIn cur = nxt;
+      nxt = load_row(it + L::NWG);
+      const float lse2 = cur.lse2;
+      const float delta = cur.delta;
+      float zs = cur.zs, cacc = cur.cacc;
       const int lim = row_ok ? (p.causal ? min(row + 1, p.Skv) : p.Skv) : 0;
       const bool masked = (m * 128 + 128 > p.Sq) || (key0 + KB > p.Skv) || (p.causal && key0 + KB - 1 > m * 128);
 

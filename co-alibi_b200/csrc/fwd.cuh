@@ -98,28 +98,47 @@ struct FwdLayout {
   static_assert(ALLOC <= 232448, "shared memory budget");
 };
 
-// Reverse scan of one 128-key score row (raw q.k dot products in sreg[]):
-// sigmoid, suffix sum carried in `run`, penalised log2-domain logit written
-// back into sreg[].  Returns the row max over the tile.  Keys >= lim are masked.
+// Reverse scan of one 32-key chunk of a score row (raw q.k dot products in
+// sreg[0..31], keys key0c..key0c+31), right to left: sigmoid, suffix sum carried
+// in `run`, penalised log2-domain logit written back into sreg[].  Folds the
+// chunk's max into mx.  Keys >= lim are masked.  Pairs of keys share packed
+// f32x2 instructions; the suffix sum itself is a scalar chain.
 template <bool MASK>
-__device__ __forceinline__ float fwd_scan_tile(uint32_t* sreg, float& run, int key0, int lim, float c_sig,
-                                               float c_a, float slope2) {
-  float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+__device__ __forceinline__ float fwd_scan_chunk(uint32_t* sreg, float& run, int key0c, int lim, float c_sig,
+                                                float c_a, float slope2, float mx) {
+  const float2 csig2 = make_float2(c_sig, c_sig), ca2 = make_float2(c_a, c_a);
+  const float2 one2 = make_float2(1.f, 1.f), nsl2 = make_float2(-slope2, -slope2);
+  // phase 1: the 32 sigmoids are independent -- issue them back to back so the
+  // MUFU pipe stays full instead of waiting on the suffix-sum chain
+  float sg[32];
 #pragma unroll
-  for (int j = 127; j >= 0; --j) {
-    const float x = __uint_as_float(sreg[j]);
-    float sg = sigmoid_from_neg_log2(x * c_sig);
-    if (MASK && key0 + j >= lim) sg = 0.f;
-    run += sg;
-    float a = fmaf(-slope2, run, x * c_a);
-    if (MASK && key0 + j >= lim) a = -INFINITY;
-    sreg[j] = __float_as_uint(a);
-    if ((j & 3) == 0) mx0 = fmaxf(mx0, a);
-    if ((j & 3) == 1) mx1 = fmaxf(mx1, a);
-    if ((j & 3) == 2) mx2 = fmaxf(mx2, a);
-    if ((j & 3) == 3) mx3 = fmaxf(mx3, a);
+  for (int q = 0; q < 16; ++q) {
+    const float2 x = make_float2(__uint_as_float(sreg[2 * q]), __uint_as_float(sreg[2 * q + 1]));
+    const float2 xn = __fmul2_rn(x, csig2);
+    const float2 y = __fadd2_rn(make_float2(ex2_approx(xn.x), ex2_approx(xn.y)), one2);
+    sg[2 * q] = rcp_approx(y.x);
+    sg[2 * q + 1] = rcp_approx(y.y);
+    if (MASK && key0c + 2 * q >= lim) sg[2 * q] = 0.f;
+    if (MASK && key0c + 2 * q + 1 >= lim) sg[2 * q + 1] = 0.f;
   }
-  return fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+  // phase 2: suffix sums (the only serial chain), then the penalised logits
+  float r[32];
+#pragma unroll
+  for (int j = 31; j >= 0; --j) {
+    run += sg[j];
+    r[j] = run;
+  }
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    const float2 x = make_float2(__uint_as_float(sreg[2 * q]), __uint_as_float(sreg[2 * q + 1]));
+    float2 a = __ffma2_rn(make_float2(r[2 * q], r[2 * q + 1]), nsl2, __fmul2_rn(x, ca2));
+    if (MASK && key0c + 2 * q >= lim) a.x = -INFINITY;
+    if (MASK && key0c + 2 * q + 1 >= lim) a.y = -INFINITY;
+    mx = max3(mx, a.x, a.y);
+    sreg[2 * q] = __float_as_uint(a.x);
+    sreg[2 * q + 1] = __float_as_uint(a.y);
+  }
+  return mx;
 }
 
 template <int D, bool BF16>
@@ -249,8 +268,6 @@ __global__ void __launch_bounds__(384, 1)
       // one waits for its MMAs the other has the exponential unit to itself.
       int k_waited = -1, v_waited = -1;
       int pv_cnt[2] = {0, 0};  // PVs issued per slot
-      int k_uses[L::KS] = {}, v_uses[L::VS] = {};
-      auto n_active = [&](int n) { return (active(0, n) ? 1 : 0) + (active(1, n) ? 1 : 0); };
       auto wait_k = [&](int n) -> bool {
         for (; k_waited < n; ++k_waited)
           if (!mbar_wait(&k_full[(k_waited + 1) % L::KS], ((k_waited + 1) / L::KS) & 1, g)) return false;
@@ -274,10 +291,8 @@ __global__ void __launch_bounds__(384, 1)
                   idS, kk > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[s]);
-        if (++k_uses[ks] == n_active(n)) {  // every active slot has read K(n): release the stage
-          k_uses[ks] = 0;
-          umma_commit(&k_empty[ks]);
-        }
+        // slot 0 always issues before slot 1 for a given n: release K(n) after the last reader
+        if (s == 1 || !active(1, n)) umma_commit(&k_empty[ks]);
         return true;
       };
       bool ok = mbar_wait(q_full, 0, g);
@@ -288,7 +303,7 @@ __global__ void __launch_bounds__(384, 1)
           const bool act = active(s, n);
           if (act) {
             // P_s(n) published by the slot's softmax warps
-            if (!(ok = mbar_wait(&p_full[s], pv_cnt[s] & 1, g))) break;
+            if (!(ok = mbar_wait_fast(&p_full[s], pv_cnt[s] & 1, g))) break;
             if (!(ok = wait_v(n))) break;
             tc_fence_after();
             const int vs = n % L::VS;
@@ -301,14 +316,14 @@ __global__ void __launch_bounds__(384, 1)
             }
             umma_commit(&pv_done[s]);
             ++pv_cnt[s];
-            if (++v_uses[vs] == n_active(n)) {
-              v_uses[vs] = 0;
-              umma_commit(&v_empty[vs]);
-            }
+            if (s == 1 || !active(1, n)) umma_commit(&v_empty[vs]);
           }
           if (n + 1 < N && active(s, n + 1)) {
-            // S_s(n+1) overwrites the columns P_s(n) is read from: wait for PV_s(n)
-            if (act && !(ok = mbar_wait(&pv_done[s], (pv_cnt[s] - 1) & 1, g))) break;
+            // S_s(n+1) overwrites the TMEM columns P_s(n) is read from.  No wait is
+            // needed: tcgen05.mma ops issued by one thread execute in issue order, so
+            // PV_s(n) has read P_s(n) before S_s(n+1) writes there (the same aliasing
+            // CUTLASS's sm100 attention mainloop relies on).  The commit that
+            // publishes S_s(n+1) also covers PV_s(n), so the softmax may rescale O.
             ok = issue_S(s, n + 1);
           }
         }
@@ -338,23 +353,24 @@ __global__ void __launch_bounds__(384, 1)
       for (int n = 0; n < N; ++n) {
         if (!active(slot, n)) continue;
         const int key0 = (last - n) * L::BN;
-        ok = mbar_wait(&s_full[slot], it & 1, g);
+        ok = mbar_wait_fast(&s_full[slot], it & 1, g);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
+        // S row in four 32-column chunks, right to left; each chunk's TMEM load
+        // overlaps the scan of the chunk to its right.
         uint32_t sreg[128];
-        tmem_ld32(lane_base, sreg);
-        tmem_ld32(lane_base + 32, sreg + 32);
-        tmem_ld32(lane_base + 64, sreg + 64);
-        tmem_ld32(lane_base + 96, sreg + 96);
-        tmem_ld_wait32(sreg);
-        tmem_ld_fence32(sreg + 32);
-        tmem_ld_fence32(sreg + 64);
-        tmem_ld_fence32(sreg + 96);
-
         const bool masked = (key0 + L::BN > p.Skv) || (p.causal && key0 + L::BN - 1 > qt * L::BM);
-        const float tmax = masked ? fwd_scan_tile<true>(sreg, run, key0, lim, c_sig, c_a, slope2)
-                                  : fwd_scan_tile<false>(sreg, run, key0, lim, c_sig, c_a, slope2);
+        float tmax = -INFINITY;
+        tmem_ld32(lane_base + 96, sreg + 96);
+        tmem_ld_wait32(sreg + 96);
+#pragma unroll
+        for (int c = 3; c >= 0; --c) {
+          if (c > 0) tmem_ld32(lane_base + 32 * (c - 1), sreg + 32 * (c - 1));
+          tmax = masked ? fwd_scan_chunk<true>(sreg + 32 * c, run, key0 + 32 * c, lim, c_sig, c_a, slope2, tmax)
+                        : fwd_scan_chunk<false>(sreg + 32 * c, run, key0 + 32 * c, lim, c_sig, c_a, slope2, tmax);
+          if (c > 0) tmem_ld_wait32(sreg + 32 * (c - 1));
+        }
         float alpha = 1.f;
         bool resc = false;
         if (m_ref == -INFINITY) {
@@ -365,7 +381,7 @@ __global__ void __launch_bounds__(384, 1)
           resc = true;
         }
         const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-        // O is free of this slot's previous PV: S_s(it) was issued only after it completed.
+        // O is free of this slot's previous PV: the commit that published S_s(it) covers it.
         if (__any_sync(0xffffffffu, resc)) {
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
@@ -377,20 +393,22 @@ __global__ void __launch_bounds__(384, 1)
             tmem_st32(lane_base + L::TM_O + c * 32, oreg);
           }
         }
-        float ls0 = 0.f, ls1 = 0.f;
+        // weights 2^(a - m) on the FMA pipe (the MUFU unit is busy with the sigmoids)
+        float2 ls = make_float2(0.f, 0.f);
+        const float2 nm = make_float2(-m_use, -m_use);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t preg[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            const float e0 = ex2_approx(__uint_as_float(sreg[32 * c + 2 * j]) - m_use);
-            const float e1 = ex2_approx(__uint_as_float(sreg[32 * c + 2 * j + 1]) - m_use);
-            ls0 += e0;
-            ls1 += e1;
-            preg[j] = pack2<BF16>(e0, e1);
+            const float2 e = exp2_poly2(__fadd2_rn(
+                make_float2(__uint_as_float(sreg[32 * c + 2 * j]), __uint_as_float(sreg[32 * c + 2 * j + 1])), nm));
+            ls = __fadd2_rn(ls, e);
+            preg[j] = pack2<BF16>(e.x, e.y);
           }
           tmem_st16(lane_base + c * 16, preg);  // P aliased over the S columns already read
         }
+        const float ls0 = ls.x, ls1 = ls.y;
         l = fmaf(l, alpha, ls0 + ls1);
         tmem_st_wait();
         tc_fence_before();

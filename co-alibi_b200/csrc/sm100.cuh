@@ -77,6 +77,38 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with an explicit suspend-time hint (ns): returns within about that
+// long even if the phase has not completed, so a polling loop built on it wakes
+// promptly (the default hint can leave a thread asleep for ~1 us after the
+// phase completes).
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait with prompt wake-up, for the waits on the critical path.
+__device__ __forceinline__ bool mbar_wait_fast(uint64_t* bar, uint32_t parity, const CtaGuard& g) {
+  if (mbar_try_wait_hint(bar, parity, 20)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait_hint(bar, parity, 20)) return true;
+    if (g.aborted()) return false;
+    if (global_timer_ns() - t0 > g.timeout_ns) {
+      g.raise(kStatusTimeout);
+      return false;
+    }
+  }
+}
+
 // Non-blocking probe (test_wait never suspends the thread, unlike try_wait).
 __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
@@ -312,6 +344,33 @@ __device__ __forceinline__ float rcp_approx(float x) {
 
 // sigmoid(p) = 1 / (1 + 2^xn) with xn = -p*log2(e): MUFU ex2 + MUFU rcp.
 __device__ __forceinline__ float sigmoid_from_neg_log2(float xn) { return rcp_approx(1.0f + ex2_approx(xn)); }
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair of x <= 0 (softmax weights) on the FMA pipe instead of the
+// MUFU unit.  x = j + f with j = round(x) taken from the low mantissa bits of
+// x + 1.5*2^23, f in [-0.5, 0.5]; 2^f from a degree-3 polynomial fitted here by
+// a minimax (Lawson-reweighted least squares) search, relative error 7.5e-5 --
+// below the float16 / bfloat16 rounding the weights get next; 2^j is added into
+// the exponent field.  x is clamped at -125 so that exponent never underflows.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 magic = make_float2(12582912.f, 12582912.f);
+  const float2 t = __fadd2_rn(x, magic);
+  const float2 j = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = __ffma2_rn(j, make_float2(-1.f, -1.f), x);
+  float2 p = __ffma2_rn(make_float2(5.517113209e-02f, 5.517113209e-02f), f,
+                        make_float2(2.426100820e-01f, 2.426100820e-01f));
+  p = __ffma2_rn(p, f, make_float2(6.932609677e-01f, 6.932609677e-01f));
+  p = __ffma2_rn(p, f, make_float2(9.999281168e-01f, 9.999281168e-01f));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
 
 template <bool BF16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi);
