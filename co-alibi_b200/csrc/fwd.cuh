@@ -67,12 +67,13 @@ __device__ __forceinline__ void decode_tile(int L, int BH, int nQ, int& bh, int&
   m = nQ - 1 - mq;
 }
 
-// Two 128-row query tiles ("slots") per CTA, ping-ponging on two softmax
-// warpgroups so that one slot's exponentials overlap the other's MMAs.
+// Two 128-row query tiles ("slots") per CTA; each slot's rows are split over
+// two warpgroups -- one thread per (row, 64-key half) -- so four softmax warps
+// share each SM sub-partition and hide each other's latencies.
 template <int D>
 struct FwdLayout {
   static constexpr int BM = 128, BN = 128;
-  static constexpr int KS = (D == 128) ? 3 : 4;
+  static constexpr int KS = (D == 128) ? 2 : 4;
   static constexpr int VS = (D == 128) ? 2 : 3;
   static constexpr int BOX = 128 * 128;  // one [128 rows][64 cols] 16-bit box, SW128
   static constexpr int TILE = BN * D * 2;
@@ -80,17 +81,20 @@ struct FwdLayout {
   static constexpr int OFF_Q = 0;  // two query tiles
   static constexpr int OFF_K = OFF_Q + 2 * QB;
   static constexpr int OFF_V = OFF_K + KS * TILE;
-  static constexpr int OFF_BAR = OFF_V + VS * TILE;
+  static constexpr int OFF_X = OFF_V + VS * TILE;  // half-row exchange: [2 parity][2 slot][2 half][128] float2
+  static constexpr int OFF_BAR = OFF_X + 2 * 2 * 2 * 128 * 8;
   static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 2 + 2 + 2 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 16;
   static constexpr int ALLOC = BYTES + 1024;
-  // warpgroups 0, 1: softmax of slot 0 / 1; warpgroup 2: TMA warp, MMA warp, two idle warps.
-  // Launched at 168 registers/thread (3 warps per SM sub-partition); the softmax
-  // warpgroups then take 232 and the producer warpgroup keeps 40: 2*232 + 40 = 3*168.
-  static constexpr int THREADS = 384;
-  static constexpr int REGS_SOFTMAX = 216, REGS_PRODUCER = 72;
-  static_assert(2 * REGS_SOFTMAX + REGS_PRODUCER <= 3 * 168, "register split exceeds the launch allocation");
+  // warps 0-15: softmax (slot = warp / 8, half = (warp / 4) % 2, lane quarter = warp % 4);
+  // warp 16: TMA producer; warp 17: TMEM allocator + MMA issuer; warps 18-19 idle.
+  // Launched at 96 registers/thread (5 warps per SM sub-partition); the softmax
+  // warpgroups then take 104 and the producer warpgroup keeps 64: 4*104 + 64 = 5*96.
+  static constexpr int THREADS = 640;
+  static constexpr int WARP_TMA = 16, WARP_MMA = 17;
+  static constexpr int REGS_SOFTMAX = 104, REGS_PRODUCER = 64;
+  static_assert(4 * REGS_SOFTMAX + REGS_PRODUCER <= 5 * 96, "register split exceeds the launch allocation");
   // TMEM per slot s at column 256*s: S [0,128) with P aliased in [0,64); O [128,128+D)
   static constexpr uint32_t TM_SLOT = 256;
   static constexpr uint32_t TM_O = 128;
@@ -98,51 +102,48 @@ struct FwdLayout {
   static_assert(ALLOC <= 232448, "shared memory budget");
 };
 
-// Reverse scan of one 32-key chunk of a score row (raw q.k dot products in
-// sreg[0..31], keys key0c..key0c+31), right to left: sigmoid, suffix sum carried
-// in `run`, penalised log2-domain logit written back into sreg[].  Folds the
-// chunk's max into mx.  Keys >= lim are masked.  Pairs of keys share packed
-// f32x2 instructions; the suffix sum itself is a scalar chain.
+// Sigmoids, local suffix sums and penalised log2-domain logits of one 64-key
+// half row (raw q.k dot products in sreg[0..63], keys key0h..key0h+63), right to
+// left, starting the suffix sum at 0.  Writes a' = c_a x - slope2 * local_suffix
+// back into sreg[]; returns the half's sigmoid total and the max of a'.
 template <bool MASK>
-__device__ __forceinline__ float fwd_scan_chunk(uint32_t* sreg, float& run, int key0c, int lim, float c_sig,
-                                                float c_a, float slope2, float mx) {
-  const float2 csig2 = make_float2(c_sig, c_sig), ca2 = make_float2(c_a, c_a);
-  const float2 one2 = make_float2(1.f, 1.f), nsl2 = make_float2(-slope2, -slope2);
-  // phase 1: the 32 sigmoids are independent -- issue them back to back so the
-  // MUFU pipe stays full instead of waiting on the suffix-sum chain
-  float sg[32];
+__device__ __forceinline__ float2 fwd_scan_half(uint32_t* sreg, int key0h, int lim, float c_sig, float c_a,
+                                                float slope2) {
+  const float2 csig2 = make_float2(c_sig, c_sig);
+  float run = 0.f, mx = -INFINITY;
 #pragma unroll
-  for (int q = 0; q < 16; ++q) {
-    const float2 x = make_float2(__uint_as_float(sreg[2 * q]), __uint_as_float(sreg[2 * q + 1]));
-    const float2 xn = __fmul2_rn(x, csig2);
-    const float2 y = __fadd2_rn(make_float2(ex2_approx(xn.x), ex2_approx(xn.y)), one2);
-    sg[2 * q] = rcp_approx(y.x);
-    sg[2 * q + 1] = rcp_approx(y.y);
-    if (MASK && key0c + 2 * q >= lim) sg[2 * q] = 0.f;
-    if (MASK && key0c + 2 * q + 1 >= lim) sg[2 * q + 1] = 0.f;
-  }
-  // phase 2: suffix sums (the only serial chain), then the penalised logits
-  float r[32];
+  for (int c = 3; c >= 0; --c) {  // 16-key groups, right to left
+    float sg[16];
 #pragma unroll
-  for (int j = 31; j >= 0; --j) {
-    run += sg[j];
-    r[j] = run;
-  }
+    for (int q = 0; q < 8; ++q) {
+      const int j = 16 * c + 2 * q;
+      const float2 xn = __fmul2_rn(make_float2(__uint_as_float(sreg[j]), __uint_as_float(sreg[j + 1])), csig2);
+      sg[2 * q] = sigmoid_from_neg_log2(xn.x);
+      sg[2 * q + 1] = sigmoid_from_neg_log2(xn.y);
+      if (MASK && key0h + j >= lim) sg[2 * q] = 0.f;
+      if (MASK && key0h + j + 1 >= lim) sg[2 * q + 1] = 0.f;
+    }
 #pragma unroll
-  for (int q = 0; q < 16; ++q) {
-    const float2 x = make_float2(__uint_as_float(sreg[2 * q]), __uint_as_float(sreg[2 * q + 1]));
-    float2 a = __ffma2_rn(make_float2(r[2 * q], r[2 * q + 1]), nsl2, __fmul2_rn(x, ca2));
-    if (MASK && key0c + 2 * q >= lim) a.x = -INFINITY;
-    if (MASK && key0c + 2 * q + 1 >= lim) a.y = -INFINITY;
-    mx = max3(mx, a.x, a.y);
-    sreg[2 * q] = __float_as_uint(a.x);
-    sreg[2 * q + 1] = __float_as_uint(a.y);
+    for (int q = 7; q >= 0; --q) {
+      const int j = 16 * c + 2 * q;
+      run += sg[2 * q + 1];
+      const float r1 = run;
+      run += sg[2 * q];
+      const float r0 = run;
+      float a0 = fmaf(-slope2, r0, __uint_as_float(sreg[j]) * c_a);
+      float a1 = fmaf(-slope2, r1, __uint_as_float(sreg[j + 1]) * c_a);
+      if (MASK && key0h + j >= lim) a0 = -INFINITY;
+      if (MASK && key0h + j + 1 >= lim) a1 = -INFINITY;
+      mx = max3(mx, a0, a1);
+      sreg[j] = __float_as_uint(a0);
+      sreg[j + 1] = __float_as_uint(a1);
+    }
   }
-  return mx;
+  return make_float2(run, mx);
 }
 
 template <int D, bool BF16>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(640, 1)
     coalibi_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
   using L = FwdLayout<D>;
@@ -152,6 +153,7 @@ __global__ void __launch_bounds__(384, 1)
   uint8_t* sQ = smem + L::OFF_Q;
   uint8_t* sK = smem + L::OFF_K;
   uint8_t* sV = smem + L::OFF_V;
+  float2* xch = reinterpret_cast<float2*>(smem + L::OFF_X);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* q_full = bars;
   uint64_t* k_full = q_full + 1;
@@ -197,14 +199,14 @@ __global__ void __launch_bounds__(384, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], 256);
       mbar_init(&pv_done[i], 1);
     }
     mbar_init(mma_idle, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 9) {
+  if (warp == L::WARP_MMA) {
     tmem_alloc(tmem_slot, L::TM_COLS);
     tmem_relinquish();
   }
@@ -213,9 +215,9 @@ __global__ void __launch_bounds__(384, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp >= 8) {
+  if (warp >= 16) {
     regs_decrease<L::REGS_PRODUCER>();
-  if (warp == 8) {
+  if (warp == L::WARP_TMA) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
@@ -255,7 +257,7 @@ __global__ void __launch_bounds__(384, 1)
         if (uses > 0) mbar_drain(&v_full[s], (uses - 1) & 1, g.timeout_ns);
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == L::WARP_MMA) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idS = make_idesc_f16(BF16, 128, L::BN, false, false);
@@ -335,18 +337,24 @@ __global__ void __launch_bounds__(384, 1)
   }
   } else {
     regs_increase<L::REGS_SOFTMAX>();
-    // ------------------------------------------------------------ softmax warpgroups 0 and 1
-    const int slot = warp >> 2;
-    const int t = threadIdx.x & 127;  // row within the slot's tile
+    // ------------------------------------------------------------ softmax: 2 slots x 2 half rows
+    const int slot = warp >> 3;
+    const int hf = (warp >> 2) & 1;   // 0: keys [64,128) of the tile (swept first), 1: keys [0,64)
+    const int quarter = warp & 3;
+    const int t = quarter * 32 + lane;  // row within the slot's tile
+    const int pair_bar = 1 + slot * 4 + quarter;  // named barrier of the two warps sharing these rows
     const int qt = 2 * pair + slot;
     const int row = qt * L::BM + t;
-    const uint32_t lane_base = tmem + slot * L::TM_SLOT + ((uint32_t)((warp & 3) * 32) << 16);
+    const uint32_t lane_base = tmem + slot * L::TM_SLOT + ((uint32_t)(quarter * 32) << 16);
+    const int scol = hf ? 0 : 64;           // my S columns (fp32)
+    const int pcol = hf ? 0 : 32;           // my packed P columns
+    const int ocol = hf ? 0 : D / 2;        // my O columns
     const float slope = load_slope(p.slopes, p.slopes_dtype, h);
     const float c_sig = -p.sm_scale * kLog2e;
     const float c_a = p.sm_scale * kLog2e;
     const float slope2 = slope * kLog2e;
     const int lim = p.causal ? min(row + 1, p.Skv) : p.Skv;
-    float m_ref = -INFINITY, l = 0.f, run = 0.f;
+    float m_ref = -INFINITY, l = 0.f, carry = 0.f;
     bool ok = true;
     int it = 0;
     if (slot == 0 || has1) {
@@ -354,23 +362,28 @@ __global__ void __launch_bounds__(384, 1)
         if (!active(slot, n)) continue;
         const int key0 = (last - n) * L::BN;
         ok = mbar_wait_fast(&s_full[slot], it & 1, g);
-        ok = __all_sync(0xffffffffu, ok);
+        ok = named_bar_and(pair_bar, 64, ok);  // both halves leave together on an abort
         if (!ok) break;
         tc_fence_after();
-        // S row in four 32-column chunks, right to left; each chunk's TMEM load
-        // overlaps the scan of the chunk to its right.
-        uint32_t sreg[128];
+        uint32_t sreg[64];
+        tmem_ld32(lane_base + scol + 32, sreg + 32);
+        tmem_ld32(lane_base + scol, sreg);
+        tmem_ld_wait32(sreg + 32);
+        tmem_ld_fence32(sreg);
         const bool masked = (key0 + L::BN > p.Skv) || (p.causal && key0 + L::BN - 1 > qt * L::BM);
-        float tmax = -INFINITY;
-        tmem_ld32(lane_base + 96, sreg + 96);
-        tmem_ld_wait32(sreg + 96);
-#pragma unroll
-        for (int c = 3; c >= 0; --c) {
-          if (c > 0) tmem_ld32(lane_base + 32 * (c - 1), sreg + 32 * (c - 1));
-          tmax = masked ? fwd_scan_chunk<true>(sreg + 32 * c, run, key0 + 32 * c, lim, c_sig, c_a, slope2, tmax)
-                        : fwd_scan_chunk<false>(sreg + 32 * c, run, key0 + 32 * c, lim, c_sig, c_a, slope2, tmax);
-          if (c > 0) tmem_ld_wait32(sreg + 32 * (c - 1));
-        }
+        const int key0h = key0 + scol;
+        const float2 loc = masked ? fwd_scan_half<true>(sreg, key0h, lim, c_sig, c_a, slope2)
+                                  : fwd_scan_half<false>(sreg, key0h, lim, c_sig, c_a, slope2);
+        // exchange (half sigmoid total, half max of a') with the partner thread of this row
+        float2* xb = xch + (it & 1) * 512 + slot * 256;
+        xb[hf * 128 + t] = loc;
+        named_bar_sync(pair_bar, 64);
+        const float2 other = xb[(1 - hf) * 128 + t];
+        const float2 right = hf ? other : loc;
+        const float2 left = hf ? loc : other;
+        const float off_r = carry, off_l = carry + right.x;
+        const float tmax = fmaxf(right.y - slope2 * off_r, left.y - slope2 * off_l);
+        carry = (carry + right.x) + left.x;
         float alpha = 1.f;
         bool resc = false;
         if (m_ref == -INFINITY) {
@@ -384,31 +397,41 @@ __global__ void __launch_bounds__(384, 1)
         // O is free of this slot's previous PV: the commit that published S_s(it) covers it.
         if (__any_sync(0xffffffffu, resc)) {
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < D / 64; ++c) {
             uint32_t oreg[32];
-            tmem_ld32(lane_base + L::TM_O + c * 32, oreg);
+            tmem_ld32(lane_base + L::TM_O + ocol + c * 32, oreg);
             tmem_ld_wait32(oreg);
 #pragma unroll
             for (int j = 0; j < 32; ++j) oreg[j] = __float_as_uint(__uint_as_float(oreg[j]) * alpha);
-            tmem_st32(lane_base + L::TM_O + c * 32, oreg);
+            tmem_st32(lane_base + L::TM_O + ocol + c * 32, oreg);
           }
         }
-        // weights 2^(a - m) on the FMA pipe (the MUFU unit is busy with the sigmoids)
-        float2 ls = make_float2(0.f, 0.f);
-        const float2 nm = make_float2(-m_use, -m_use);
+        // e = 2^(a' - slope2 * my_offset - m)
+        const float shift = m_use + slope2 * (hf ? off_l : off_r);
+        float ls0 = 0.f, ls1 = 0.f;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t preg[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            const float2 e = exp2_poly2(__fadd2_rn(
-                make_float2(__uint_as_float(sreg[32 * c + 2 * j]), __uint_as_float(sreg[32 * c + 2 * j + 1])), nm));
-            ls = __fadd2_rn(ls, e);
-            preg[j] = pack2<BF16>(e.x, e.y);
+            // half of the exponentials on the MUFU unit, half as a polynomial on the FMA pipe
+            float e0, e1;
+            if (j & 1) {
+              const float2 e = exp2_poly2(__fadd2_rn(
+                  make_float2(__uint_as_float(sreg[32 * c + 2 * j]), __uint_as_float(sreg[32 * c + 2 * j + 1])),
+                  make_float2(-shift, -shift)));
+              e0 = e.x;
+              e1 = e.y;
+            } else {
+              e0 = ex2_approx(__uint_as_float(sreg[32 * c + 2 * j]) - shift);
+              e1 = ex2_approx(__uint_as_float(sreg[32 * c + 2 * j + 1]) - shift);
+            }
+            ls0 += e0;
+            ls1 += e1;
+            preg[j] = pack2<BF16>(e0, e1);
           }
-          tmem_st16(lane_base + c * 16, preg);  // P aliased over the S columns already read
+          tmem_st16(lane_base + pcol + c * 16, preg);  // P aliased over the S columns already read
         }
-        const float ls0 = ls.x, ls1 = ls.y;
         l = fmaf(l, alpha, ls0 + ls1);
         tmem_st_wait();
         tc_fence_before();
@@ -416,35 +439,41 @@ __global__ void __launch_bounds__(384, 1)
         ++it;
       }
       if (ok && it > 0) {
+        // combine the two halves' row sums, then wait for the last PV
+        float2* xb = xch + (it & 1) * 512 + slot * 256;
+        xb[hf * 128 + t] = make_float2(l, 0.f);
+        named_bar_sync(pair_bar, 64);
+        const float l_other = xb[(1 - hf) * 128 + t].x;
+        const float l_row = hf ? (l_other + l) : (l + l_other);  // right + left in both threads
         ok = mbar_wait(&pv_done[slot], (it - 1) & 1, g);
         ok = __all_sync(0xffffffffu, ok);
-      }
-      if (ok && it > 0) {
-        tc_fence_after();
-        const float inv = 1.0f / (l + 1e-9f);
-        uint8_t* orow = static_cast<uint8_t*>(p.o) + ((size_t)bh * p.Sq + row) * D * 2;
+        if (ok) {
+          tc_fence_after();
+          const float inv = 1.0f / (l_row + 1e-9f);
+          uint8_t* orow = static_cast<uint8_t*>(p.o) + ((size_t)bh * p.Sq + row) * D * 2 + ocol * 2;
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t oreg[32];
-          tmem_ld32(lane_base + L::TM_O + c * 32, oreg);
-          tmem_ld_wait32(oreg);
-          if (row < p.Sq) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
+          for (int c = 0; c < D / 64; ++c) {
+            uint32_t oreg[32];
+            tmem_ld32(lane_base + L::TM_O + ocol + c * 32, oreg);
+            tmem_ld_wait32(oreg);
+            if (row < p.Sq) {
+              uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
 #pragma unroll
-            for (int v4 = 0; v4 < 4; ++v4) {
-              uint4 pk;
-              pk.x = pack2<BF16>(__uint_as_float(oreg[8 * v4 + 0]) * inv, __uint_as_float(oreg[8 * v4 + 1]) * inv);
-              pk.y = pack2<BF16>(__uint_as_float(oreg[8 * v4 + 2]) * inv, __uint_as_float(oreg[8 * v4 + 3]) * inv);
-              pk.z = pack2<BF16>(__uint_as_float(oreg[8 * v4 + 4]) * inv, __uint_as_float(oreg[8 * v4 + 5]) * inv);
-              pk.w = pack2<BF16>(__uint_as_float(oreg[8 * v4 + 6]) * inv, __uint_as_float(oreg[8 * v4 + 7]) * inv);
-              dst[v4] = pk;
+              for (int v4 = 0; v4 < 4; ++v4) {
+                uint4 pk;
+                pk.x = pack2<BF16>(__uint_as_float(oreg[8 * v4 + 0]) * inv, __uint_as_float(oreg[8 * v4 + 1]) * inv);
+                pk.y = pack2<BF16>(__uint_as_float(oreg[8 * v4 + 2]) * inv, __uint_as_float(oreg[8 * v4 + 3]) * inv);
+                pk.z = pack2<BF16>(__uint_as_float(oreg[8 * v4 + 4]) * inv, __uint_as_float(oreg[8 * v4 + 5]) * inv);
+                pk.w = pack2<BF16>(__uint_as_float(oreg[8 * v4 + 6]) * inv, __uint_as_float(oreg[8 * v4 + 7]) * inv);
+                dst[v4] = pk;
+              }
             }
           }
-        }
-        if (row < p.Sq) {
-          const size_t ri = (size_t)bh * p.Sq + row;
-          p.lse[ri] = m_ref * kLn2 + logf(l + 1e-9f);
-          p.rowsig[ri] = run;
+          if (row < p.Sq && hf == 0) {
+            const size_t ri = (size_t)bh * p.Sq + row;
+            p.lse[ri] = m_ref * kLn2 + logf(l_row + 1e-9f);
+            p.rowsig[ri] = carry;
+          }
         }
       }
     }
@@ -453,7 +482,7 @@ __global__ void __launch_bounds__(384, 1)
   __syncwarp();
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == L::WARP_MMA) {
     tc_fence_after();
     tmem_dealloc(tmem, L::TM_COLS);
   }
