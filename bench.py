@@ -44,7 +44,7 @@ CONFIGS = {
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of each
 # kernel at cfg2: one ncu capture at B=2 (profiles/<kernel>_kernel_cfg2_b2_ncu_full.txt)
 # scaled by 4 to the B=8 launch (traffic grows with the number of (b, h) units).
-NCU_TRAFFIC_CFG2 = {"fwd": 4 * 116.226e6, "bwd_a": 4 * 179.122e6, "bwd_b": 4 * 216.989e6, "bwd_delta": None}
+NCU_TRAFFIC_CFG2 = {"fwd": 4 * 114.8e6, "bwd_a": 4 * 202.6e6, "bwd_b": 4 * 254.2e6, "bwd_delta": None}
 
 
 def visible(S, causal):
@@ -214,8 +214,8 @@ def config_dict(args, cfg):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
@@ -378,7 +378,9 @@ def main():
     burst, sustained, hbm, peak_src = load_peaks()
     per_kernel_flops = {"fwd": 4.0 * D * E, "bwd_a": 6.0 * D * E, "bwd_b": 8.0 * D * E,
                         "bwd_delta": 0.0}
-    per_kernel_mufu = {"fwd": 3.0 * E, "bwd_a": 3.0 * E, "bwd_b": 3.0 * E, "bwd_delta": 0.0}
+    # MUFU ops per visible score: forward = tanh sigmoid + half of the exp2 (the other
+    # half runs as a polynomial on the FMA pipe); backward passes = tanh + exp2
+    per_kernel_mufu = {"fwd": 1.5 * E, "bwd_a": 2.0 * E, "bwd_b": 2.0 * E, "bwd_delta": 0.0}
     dom = max(kern_ms, key=kern_ms.get)
     ach = per_kernel_flops[dom] / (kern_ms[dom] * 1e-3) / 1e12
     sm_mhz = clocks["sm_mhz"] if clocks else 1965.0
@@ -395,7 +397,7 @@ def main():
             "flops_per_launch": per_kernel_flops[dom],
             "note": "algorithmic FLOPs on causal-visible scores of the kernel's GEMMs "
                     "(fwd 4D, pass A 6D, pass B 8D per score) / mean CUDA-event duration in the timed region; "
-                    "second roofline: mufu_frac = 3 MUFU ops per score / (16 ops/clk/SM x 148 SMs x sampled clock)"}
+                    "second roofline: mufu_frac = MUFU ops per score (fwd 1.5, pass A/B 2) / (16 ops/clk/SM x 148 SMs x sampled clock)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -408,7 +410,7 @@ def main():
             "metric": metric_name(args.config), "value": round(value, 3), "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4),
             "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
-            "dtype": str(dtype).split(".")[-1].replace("float16", "fp16").replace("bfloat16", "bf16"),
+            "dtype": {torch.float16: "fp16", torch.bfloat16: "bf16"}[dtype],
             "data": "synthetic", "config": config_dict(args, cfg),
             "fwd_ms": round(fwd_ms, 4) if fwd_ms else None,
             "fwd_tflops": round(flops_fwd / (fwd_ms * 1e-3) / 1e12, 3) if fwd_ms else None,

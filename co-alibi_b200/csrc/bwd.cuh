@@ -41,10 +41,10 @@ struct BwdWorkspace {
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// delta: float [B*Hq][sq_pad];  carry: float2 [B*Hq][n_kb64][sq_pad]
+// delta: float [B*Hq][sq_pad];  carry: float2 [B*Hq][n_kb32][sq_pad] (one pair per 32 keys)
 inline BwdWorkspace bwd_workspace_layout(int B, int Hq, int Sq, int Skv) {
   const size_t sq_pad = (size_t)((Sq + 127) / 128) * 128;
-  const size_t nkb = (size_t)((Skv + 63) / 64);
+  const size_t nkb = (size_t)((Skv + 31) / 32);
   BwdWorkspace w;
   w.delta_off = 0;
   w.carry_off = align256((size_t)B * Hq * sq_pad * 4);
@@ -71,7 +71,8 @@ struct BwdParams {
   unsigned long long timeout_ns;
   int n_qtiles;   // ceil(Sq / 128)
   int n_kvtiles;  // ceil(Skv / 128)
-  int n_kb64;     // ceil(Skv / 64)
+  int n_kb64;     // ceil(Skv / 64): pass A's 64-key sub-tiles
+  int n_kb32;     // ceil(Skv / 32): carry entries per row
   int n_blocks;   // pass-B key blocks: ceil(Skv / KB)
   int sq_pad;
 };
@@ -260,14 +261,14 @@ __global__ void __launch_bounds__(320, 1)
       int nk = 0, nv = 0;
       for (int n = 0; n < N; ++n) {
         const int ks = n % L::KS;
-        if (!mbar_wait(&k_empty[ks], ((n / L::KS) & 1) ^ 1, g)) break;
+        if (!mbar_wait_fast(&k_empty[ks], ((n / L::KS) & 1) ^ 1, g)) break;
         mbar_arrive_expect_tx(&k_full[ks], L::TILE);
 #pragma unroll
         for (int bx = 0; bx < D / 64; ++bx)
           tma_load_3d(sK + ks * L::TILE + bx * L::KBOX, &tmK, &k_full[ks], bx * 64, n * L::BN, zkv);
         ++nk;
         const int vs = n % L::VS;
-        if (!mbar_wait(&v_empty[vs], ((n / L::VS) & 1) ^ 1, g)) break;
+        if (!mbar_wait_fast(&v_empty[vs], ((n / L::VS) & 1) ^ 1, g)) break;
         mbar_arrive_expect_tx(&v_full[vs], L::TILE);
 #pragma unroll
         for (int bx = 0; bx < D / 64; ++bx)
@@ -373,7 +374,7 @@ __global__ void __launch_bounds__(320, 1)
     const int lim = row_ok ? (p.causal ? min(row + 1, p.Skv) : p.Skv) : 0;
     const bool rows_partial = (qt * L::BM + L::BM > p.Sq);
     float cacc = 0.f;
-    float2* carry_row = p.carry + (size_t)bh * p.n_kb64 * p.sq_pad + row;
+    float2* carry_row = p.carry + (size_t)bh * p.n_kb32 * p.sq_pad + row;
     bool ok = true;
     int it = 0;
     if (slot == 0 || has1) {
@@ -384,7 +385,6 @@ __global__ void __launch_bounds__(320, 1)
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
-        carry_row[(size_t)n * p.sq_pad] = make_float2(zs, cacc);
         const bool masked =
             rows_partial || (key0 + L::BN > p.Skv) || (p.causal && key0 + L::BN - 1 > qt * L::BM);
 #pragma unroll 1
@@ -394,6 +394,7 @@ __global__ void __launch_bounds__(320, 1)
           tmem_ld32(lane_base + L::TM_DS + c * 32, dsreg);
           tmem_ld_wait32(sreg);
           tmem_ld_fence32(dsreg);
+          if (2 * n + c < p.n_kb32) carry_row[(size_t)(2 * n + c) * p.sq_pad] = make_float2(zs, cacc);
           uint32_t dpo[16];
           if (masked)
             bwd_chunk<true, BF16, false>(sreg, dsreg, key0 + c * 32, lim, c_sig, c_a, slope, slope2, lse2, delta,
@@ -455,7 +456,10 @@ struct BwdBLayout {
   static constexpr bool TRANS = (D == 128);      // accumulate dV^T / dK^T (M = D)
   static constexpr int KB = TRANS ? 64 : 128;    // keys per CTA
   static constexpr int NS = TRANS ? 2 : 1;       // S / dS TMEM buffers
-  static constexpr int NWG = NS;                 // softmax warpgroups; WG w takes iterations it % NWG == w
+  // D = 128: two softmax warpgroups work on every iteration together, warpgroup w
+  // on keys [32w, 32w+32) of the block (pass A's carries every 32 keys make the
+  // halves independent).  D = 64: one warpgroup, all 128 keys.
+  static constexpr int NWG = NS;
   static constexpr int THREADS = 128 * NWG + 64; // + TMA warp + MMA warp
   static constexpr int WARP_TMA = 4 * NWG, WARP_MMA = 4 * NWG + 1;
   static constexpr int QS = 2, PS = 2;           // Q/dO and P/dP shared-memory stages
@@ -538,7 +542,7 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
       mbar_init(&qdo_empty[i], 1);
     }
     for (int i = 0; i < L::PS; ++i) {
-      mbar_init(&pp_full[i], 128);
+      mbar_init(&pp_full[i], 128 * L::NWG);
       mbar_init(&pp_empty[i], 1);
     }
     mbar_init(&s_full[0], 1);
@@ -576,7 +580,7 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
         const int m = m_start + it % nM;
         const int bhq = b * p.Hq + hh;
         const int st = it % L::QS;
-        if (!mbar_wait(&qdo_empty[st], ((it / L::QS) & 1) ^ 1, g)) break;
+        if (!mbar_wait_fast(&qdo_empty[st], ((it / L::QS) & 1) ^ 1, g)) break;
         mbar_arrive_expect_tx(&qdo_full[st], 2 * L::QB);
         uint8_t* sq = sQDO + st * 2 * L::QB;
 #pragma unroll
@@ -705,7 +709,10 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const float c_sig = -p.sm_scale * kLog2e;
     const float c_a = p.sm_scale * kLog2e;
-    const int kb64 = key0 / 64;
+    // keys of the block this thread covers: [key0 + wkey0, key0 + wkey0 + WKB)
+    constexpr int WKB = KB / L::NWG;
+    const int wkey0 = wg * WKB;
+    const int kb32 = (key0 + wkey0) / 32;
     bool ok = true;
     // Per-row inputs of an iteration (lse, delta, and pass A's carries at this key
     // block) are loaded one iteration ahead so their latency overlaps the current
@@ -722,13 +729,13 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
       const int row_ = m_ * 128 + t_row;
       if (row_ < p.Sq) r.lse2 = p.lse[(size_t)bhq_ * p.Sq + row_] * kLog2e;
       r.delta = p.delta[(size_t)bhq_ * p.sq_pad + row_];
-      const float2 cin = p.carry[((size_t)bhq_ * p.n_kb64 + kb64) * p.sq_pad + row_];
+      const float2 cin = p.carry[((size_t)bhq_ * p.n_kb32 + kb32) * p.sq_pad + row_];
       r.zs = cin.x;
       r.cacc = cin.y;
       return r;
     };
-    RowIn nxt = load_row(wg);
-    for (int it = wg; it < NIT; it += L::NWG) {
+    RowIn nxt = load_row(0);
+    for (int it = 0; it < NIT; ++it) {
       const int hh = gkv * G + it / nM;
       const int m = m_start + it % nM;
       const int row = m * 128 + t_row;
@@ -736,12 +743,14 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
       const float slope = load_slope(p.slopes, p.slopes_dtype, hh);
       const float slope2 = slope * kLog2e;
       const RowIn cur = nxt;
-      nxt = load_row(it + L::NWG);
+      nxt = load_row(it + 1);
       const float lse2 = cur.lse2;
       const float delta = cur.delta;
       float zs = cur.zs, cacc = cur.cacc;
       const int lim = row_ok ? (p.causal ? min(row + 1, p.Skv) : p.Skv) : 0;
-      const bool masked = (m * 128 + 128 > p.Sq) || (key0 + KB > p.Skv) || (p.causal && key0 + KB - 1 > m * 128);
+      const int mkey0 = key0 + wkey0;
+      const bool masked =
+          (m * 128 + 128 > p.Sq) || (mkey0 + WKB > p.Skv) || (p.causal && mkey0 + WKB - 1 > m * 128);
 
       const int sb = it % L::NS;
       ok = mbar_wait(&s_full[sb], (it / L::NS) & 1, g);
@@ -755,27 +764,28 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
       const uint32_t rsw = t_row & 7;
       const uint32_t rbase = (t_row >> 3) * 1024 + rsw * 128;
 #pragma unroll 1
-      for (int c = 0; c < KB / 32; ++c) {
+      for (int c = 0; c < WKB / 32; ++c) {
+        const int kc = wkey0 / 32 + c;  // 32-key chunk index within the block
         uint32_t sreg[32], dsreg[32];
-        tmem_ld32(lane_base + L::TM_S + sb * KB + c * 32, sreg);
-        tmem_ld32(lane_base + L::TM_DS + sb * KB + c * 32, dsreg);
+        tmem_ld32(lane_base + L::TM_S + sb * KB + kc * 32, sreg);
+        tmem_ld32(lane_base + L::TM_DS + sb * KB + kc * 32, dsreg);
         tmem_ld_wait32(sreg);
         tmem_ld_fence32(dsreg);
-        if (L::NS == 1 && c == KB / 32 - 1) {
+        if (L::NS == 1 && c == WKB / 32 - 1) {
           tc_fence_before();
           mbar_arrive(s_free);
         }
         uint32_t po[16], dpo[16];
         if (masked)
-          bwd_chunk<true, BF16, true>(sreg, dsreg, key0 + c * 32, lim, c_sig, c_a, slope, slope2, lse2, delta, zs,
-                                      cacc, dpo, po);
+          bwd_chunk<true, BF16, true>(sreg, dsreg, key0 + kc * 32, lim, c_sig, c_a, slope, slope2, lse2, delta,
+                                      zs, cacc, dpo, po);
         else
-          bwd_chunk<false, BF16, true>(sreg, dsreg, key0 + c * 32, lim, c_sig, c_a, slope, slope2, lse2, delta,
+          bwd_chunk<false, BF16, true>(sreg, dsreg, key0 + kc * 32, lim, c_sig, c_a, slope, slope2, lse2, delta,
                                        zs, cacc, dpo, po);
         // 32 keys = four 16-byte chunks; 64-key swizzle rows, 128x128-byte blocks
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int chunk = c * 4 + u;          // 8-key chunk index within the KB keys
+          const int chunk = kc * 4 + u;          // 8-key chunk index within the KB keys
           const uint32_t blk64 = chunk >> 3;    // which 64-key block
           const uint32_t cc = chunk & 7;
           const uint32_t off = blk64 * (128 * 128) + rbase + ((cc ^ rsw) << 4);
@@ -788,9 +798,10 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
       tc_fence_before();
       mbar_arrive(&pp_full[ps]);
     }
-    // epilogue (warpgroup 0 covers all 128 TMEM lanes)
+    // epilogue: every warpgroup covers all 128 TMEM lanes; with two warpgroups
+    // (transposed accumulators, lanes = d) each writes its half of the key columns
     const int bkv = hk;
-    if (wg != 0) {
+    if (!L::TRANS && wg != 0) {
     } else if (NIT > 0) {
       if (ok) {
         ok = mbar_wait(acc_done, 0, g);
@@ -802,7 +813,7 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
           // lane t = d; columns = keys of this block
           const int d = t_row;
 #pragma unroll 1
-          for (int c = 0; c < KB / 32; ++c) {
+          for (int c = wkey0 / 32; c < (wkey0 + WKB) / 32; ++c) {
             uint32_t rv[32], rk[32];
             tmem_ld32(lane_base + L::TM_DV + c * 32, rv);
             tmem_ld32(lane_base + L::TM_DK + c * 32, rk);
@@ -856,7 +867,7 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
       // no query row sees these keys: their gradients are zero
       if (L::TRANS) {
         const int d = t_row;
-        for (int j = 0; j < KB; ++j) {
+        for (int j = wkey0; j < wkey0 + WKB; ++j) {
           const int key = key0 + j;
           if (key < p.Skv) {
             const size_t o = ((size_t)bkv * p.Skv + key) * D + d;
@@ -864,7 +875,7 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
             static_cast<uint16_t*>(p.dk)[o] = 0;
           }
         }
-      } else {
+      } else if (wg == 0) {
         const int key = key0 + t_row;
         if (key < p.Skv) {
           uint4* dvrow = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.dv) + ((size_t)bkv * p.Skv + key) * D * 2);
@@ -937,6 +948,7 @@ inline int bwd_launch_t(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigne
   p.n_qtiles = (a.Sq + 127) / 128;
   p.n_kvtiles = (a.Skv + 127) / 128;
   p.n_kb64 = (a.Skv + 63) / 64;
+  p.n_kb32 = (a.Skv + 31) / 32;
   p.n_blocks = (a.Skv + BwdBLayout<D>::KB - 1) / BwdBLayout<D>::KB;
   p.sq_pad = p.n_qtiles * 128;
 

@@ -232,14 +232,14 @@ __global__ void __launch_bounds__(640, 1)
       for (int n = 0; n < N; ++n) {
         const int key0 = (last - n) * L::BN;
         const int ks = n % L::KS;
-        if (!mbar_wait(&k_empty[ks], ((n / L::KS) & 1) ^ 1, g)) break;
+        if (!mbar_wait_fast(&k_empty[ks], ((n / L::KS) & 1) ^ 1, g)) break;
         mbar_arrive_expect_tx(&k_full[ks], L::TILE);
 #pragma unroll
         for (int bx = 0; bx < D / 64; ++bx)
           tma_load_3d(sK + ks * L::TILE + bx * L::BOX, &tmK, &k_full[ks], bx * 64, key0, zkv);
         ++nk;
         const int vs = n % L::VS;
-        if (!mbar_wait(&v_empty[vs], ((n / L::VS) & 1) ^ 1, g)) break;
+        if (!mbar_wait_fast(&v_empty[vs], ((n / L::VS) & 1) ^ 1, g)) break;
         mbar_arrive_expect_tx(&v_full[vs], L::TILE);
 #pragma unroll
         for (int bx = 0; bx < D / 64; ++bx)

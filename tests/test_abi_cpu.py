@@ -33,11 +33,12 @@ def test_strerror_and_workspace_size():
     for code in range(0, 11):
         assert _lib.strerror(code)
     assert "head dim" in _lib.strerror(2)
-    sq_pad, nkb = 4096, 64
+    # delta: float per (b, h, padded row); carries: float2 per (b, h, 32-key block, padded row)
+    sq_pad, nkb = 4096, 4096 // 32
     want = 8 * 16 * sq_pad * 4 + 8 * 16 * nkb * sq_pad * 8
     assert lib.coalibi_bwd_workspace_bytes(8, 16, 16, 4096, 4096, 128) == want
     assert lib.coalibi_bwd_workspace_bytes(1, 4, 4, 37, 37, 64) == 256 * ((4 * 128 * 4 + 255) // 256) + \
-        256 * ((4 * 1 * 128 * 8 + 255) // 256)
+        256 * ((4 * 2 * 128 * 8 + 255) // 256)
     assert lib.coalibi_bwd_workspace_bytes(0, 4, 4, 37, 37, 64) == 0
 
 
