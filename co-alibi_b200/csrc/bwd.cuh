@@ -71,7 +71,6 @@ struct BwdParams {
   unsigned long long timeout_ns;
   int n_qtiles;   // ceil(Sq / 128)
   int n_kvtiles;  // ceil(Skv / 128)
-  int n_kb64;     // ceil(Skv / 64): pass A's 64-key sub-tiles
   int n_kb32;     // ceil(Skv / 32): carry entries per row
   int n_blocks;   // pass-B key blocks: ceil(Skv / KB)
   int sq_pad;
@@ -147,73 +146,152 @@ __device__ __forceinline__ void bwd_chunk(const uint32_t* sreg, const uint32_t* 
 }
 
 // ---------------------------------------------------------------------------
-// 2. pass A: dQ and the per-64-key carries
+// 2. pass A: dQ and the per-32-key carries
 //
-// Two 128-row query tiles ("slots") per CTA on two softmax warpgroups; key
-// sub-tiles of 64, left to right.  TMEM per slot s (column 256*s): S [0,64)
-// with dP aliased over its first 32 columns once read, dS [64,128), dQ [128,128+D).
+// One 128-row query tile per CTA; key sub-tiles of 128, left to right, so every
+// MMA has N = 128 (an N = 64 tile reads its A operand from shared memory for
+// half the work).  Four softmax warpgroups split each sub-tile's keys 32 ways
+// (warpgroup w: keys [32w, 32w+32)).  The running sums along a row (sigmoid
+// suffix, dA prefix) are handed from warpgroup to warpgroup through shared
+// memory and per-link mbarriers: w passes its running value to w+1 as soon as
+// its own chunk total is known, and warpgroup 3 passes it on to warpgroup 0 for
+// the next sub-tile.  No warpgroup waits for one to its right, so the four warps
+// on a sub-partition drift apart and overlap their MUFU-bound and FMA-bound
+// phases.  Each thread copies its S and dP columns to registers and
+// releases them at once, so the MMA warp computes S/dP of the next sub-tile
+// while this one is still in the softmax.  TMEM: S [0,128), dP [128,256),
+// dS (packed 16-bit) [256,320), dQ [320,320+D).
 // ---------------------------------------------------------------------------
 template <int D>
 struct BwdALayout {
-  static constexpr int BM = 128, BN = 64;
-  static constexpr int KS = 3, VS = 2;
-  static constexpr int QBOX = 128 * 128;   // [128 rows][64 cols] box
-  static constexpr int KBOX = BN * 128;    // [64 rows][64 cols] box
-  static constexpr int TILE = BN * D * 2;  // one 64-key K or V sub-tile
+  static constexpr int BM = 128, BN = 128;
+  static constexpr int NWG = 4;                  // softmax warpgroups, 32 keys each
+  static constexpr int KS = (D == 128) ? 3 : 4;  // K lives from S(n) to dQ(n): deeper ring
+  static constexpr int VS = (D == 128) ? 1 : 2;  // V only feeds dP(n)
+  static constexpr int KBOX = BN * 128;          // [128 rows][64 cols] box
+  static constexpr int TILE = BN * D * 2;        // one K or V sub-tile
   static constexpr int QB = BM * D * 2;
-  static constexpr int OFF_Q = 0;          // Q slot 0, Q slot 1, dO slot 0, dO slot 1
-  static constexpr int OFF_K = 4 * QB;
+  static constexpr int OFF_Q = 0, OFF_DO = QB;
+  static constexpr int OFF_K = 2 * QB;
   static constexpr int OFF_V = OFF_K + KS * TILE;
-  static constexpr int OFF_BAR = OFF_V + VS * TILE;
-  static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 2 + 2 + 2 + 1;
+  static constexpr int OFF_X = OFF_V + VS * TILE;  // float [2][NWG][128]: running sums handed to warpgroup w
+  static constexpr int OFF_BAR = OFF_X + 2 * NWG * 128 * 4;
+  static constexpr int NLINK = 4 * NWG;            // per (lane quarter, receiving warpgroup)
+  static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 7 + 2 * NLINK;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 16;
   static constexpr int ALLOC = BYTES + 1024;
-  static constexpr int THREADS = 320;      // 2 softmax warpgroups + TMA warp + MMA warp
-  static constexpr int WARP_TMA = 8, WARP_MMA = 9;
-  static constexpr uint32_t TM_SLOT = 256, TM_S = 0, TM_DS = 64, TM_DQ = 128, TM_COLS = 512;
+  // + a producer warpgroup (TMA warp, MMA warp, two idle).  640 threads put five
+  // warps on each SM sub-partition (96 registers each at launch); setmaxnreg then
+  // moves registers from the producer warpgroup to the softmax.
+  static constexpr int THREADS = 128 * NWG + 128;
+  static constexpr int WARP_TMA = 4 * NWG, WARP_MMA = 4 * NWG + 1;
+  static constexpr int REGS_SOFTMAX = 104, REGS_PRODUCER = 64;
+  static_assert(4 * REGS_SOFTMAX + REGS_PRODUCER <= 5 * 96, "register split exceeds the launch allocation");
+  static constexpr uint32_t TM_S = 0, TM_DP = 128, TM_DS = 256, TM_DQ = 320, TM_COLS = 512;
   static_assert(ALLOC <= 232448, "shared memory budget");
+  static_assert(TM_DQ + D <= TM_COLS, "TMEM budget");
 };
 
+// Per-key maths of pass A, two keys per packed f32x2 instruction (one issue
+// slot for two lanes of work; the softmax warps are issue-bound).
+//
+// Phase 1 of a 32-key chunk: sigmoids (kept in sg) and p*c_a - lse2 (kept in xa,
+// over the S registers); returns the chunk's sigmoid total.
+template <bool MASK>
+__device__ __forceinline__ float bwd_a_sig(uint32_t* sreg, float* sg, int key0, int lim, float c_t, float c_a,
+                                           float lse2) {
+  float2 tot = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    const float2 x = make_float2(__uint_as_float(sreg[j]), __uint_as_float(sreg[j + 1]));
+    const float2 u = __fmul2_rn(x, make_float2(c_t, c_t));
+    float2 sv = __ffma2_rn(make_float2(0.5f, 0.5f), make_float2(tanh_approx(u.x), tanh_approx(u.y)),
+                           make_float2(0.5f, 0.5f));
+    if (MASK && key0 + j >= lim) sv.x = 0.f;
+    if (MASK && key0 + j + 1 >= lim) sv.y = 0.f;
+    sg[j] = sv.x;
+    sg[j + 1] = sv.y;
+    tot = __fadd2_rn(tot, sv);
+    const float2 xa = __ffma2_rn(x, make_float2(c_a, c_a), make_float2(-lse2, -lse2));
+    sreg[j] = __float_as_uint(xa.x);
+    sreg[j + 1] = __float_as_uint(xa.y);
+  }
+  return tot.x + tot.y;
+}
+
+// Phase 2 on 16 keys: P from the sigmoid suffix zz, dA = P (dP - delta) over the
+// xa registers; returns the sum of dA.
+template <bool MASK>
+__device__ __forceinline__ float bwd_a_da(uint32_t* xa, const float* sg, const uint32_t* dpr, int key0, int lim,
+                                          float slope2, float delta, float& zz) {
+  float2 tot = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < 16; j += 2) {
+    float2 z;
+    z.x = zz;
+    zz -= sg[j];
+    z.y = zz;
+    zz -= sg[j + 1];
+    const float2 e = __ffma2_rn(make_float2(-slope2, -slope2), z,
+                                make_float2(__uint_as_float(xa[j]), __uint_as_float(xa[j + 1])));
+    float2 P;
+    P.x = ex2_approx(e.x);
+    P.y = ex2_approx(e.y);
+    if (MASK && key0 + j >= lim) P.x = 0.f;
+    if (MASK && key0 + j + 1 >= lim) P.y = 0.f;
+    const float2 dA = __fmul2_rn(
+        P, __fadd2_rn(make_float2(__uint_as_float(dpr[j]), __uint_as_float(dpr[j + 1])), make_float2(-delta, -delta)));
+    xa[j] = __float_as_uint(dA.x);
+    xa[j + 1] = __float_as_uint(dA.y);
+    tot = __fadd2_rn(tot, dA);
+  }
+  return tot.x + tot.y;
+}
+
 template <int D, bool BF16>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
     coalibi_bwd_a_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
                          const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                          const BwdParams p) {
   using L = BwdALayout<D>;
+  constexpr int BN = L::BN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem + L::OFF_Q;  // slot s: Q at s*QB, dO at (2+s)*QB
+  uint8_t* sQ = smem + L::OFF_Q;
+  uint8_t* sDO = smem + L::OFF_DO;
   uint8_t* sK = smem + L::OFF_K;
   uint8_t* sV = smem + L::OFF_V;
+  float* xs = reinterpret_cast<float*>(smem + L::OFF_X);  // [NWG][128] sigmoid suffix at chunk start
+  float* xd = xs + L::NWG * 128;                          // [NWG][128] dA prefix at chunk start
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* q_full = bars;
   uint64_t* k_full = q_full + 1;
   uint64_t* k_empty = k_full + L::KS;
   uint64_t* v_full = k_empty + L::KS;
   uint64_t* v_empty = v_full + L::VS;
-  uint64_t* s_full = v_empty + L::VS;  // [2]
-  uint64_t* dp_full = s_full + 2;      // [2]
-  uint64_t* dq_done = dp_full + 2;     // [2]
-  uint64_t* mma_idle = dq_done + 2;
+  uint64_t* s_full = v_empty + L::VS;
+  uint64_t* s_free = s_full + 1;   // every softmax warp has S in registers
+  uint64_t* dp_full = s_free + 1;
+  uint64_t* dp_free = dp_full + 1;
+  uint64_t* ds_full = dp_free + 1;  // dS of the sub-tile written to TMEM
+  uint64_t* dq_done = ds_full + 1;
+  uint64_t* mma_idle = dq_done + 1;
+  uint64_t* zlink = mma_idle + 1;      // [quarter][receiving warpgroup]
+  uint64_t* clink = zlink + L::NLINK;  // [quarter][receiving warpgroup]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
   const int warp = warp_id();
   const int lane = lane_id();
   const int BH = p.B * p.Hq;
-  const int n_pairs = (p.n_qtiles + 1) / 2;
-  int bh, pair;
-  decode_tile(blockIdx.x, BH, n_pairs, bh, pair);
+  int bh, qt;
+  decode_tile(blockIdx.x, BH, p.n_qtiles, bh, qt);
   const int b = bh / p.Hq;
   const int h = bh - b * p.Hq;
   const int zkv = b * p.Hkv + h / (p.Hq / p.Hkv);
-  const bool has1 = (2 * pair + 1) < p.n_qtiles;
-  // last 64-key sub-tile each slot visits (causal: sub-tiles starting at or before its last row)
-  const int last0 = p.causal ? min(p.n_kb64 - 1, (2 * pair) * 2 + 1) : p.n_kb64 - 1;
-  const int last1 = has1 ? (p.causal ? min(p.n_kb64 - 1, (2 * pair + 1) * 2 + 1) : p.n_kb64 - 1) : -1;
-  const int N = max(last0, last1) + 1;
-  auto active = [&](int s, int n) -> bool { return n <= (s == 0 ? last0 : last1); };
+  // 128-key sub-tiles this query tile sees (causal: those starting at or before its last row)
+  const int N = p.causal ? min(p.n_kvtiles, qt + 1) : p.n_kvtiles;
   CtaGuard g{abort_flag, p.status, p.timeout_ns};
 
   if (threadIdx.x == 0) {
@@ -226,12 +304,17 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&dp_full[i], 128);
-      mbar_init(&dq_done[i], 1);
-    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 4 * L::NWG);
+    mbar_init(dp_full, 1);
+    mbar_init(dp_free, 4 * L::NWG);
+    mbar_init(ds_full, 4 * L::NWG);
+    mbar_init(dq_done, 1);
     mbar_init(mma_idle, 1);
+    for (int i = 0; i < L::NLINK; ++i) {
+      mbar_init(&zlink[i], 32);  // every lane of the sending warp arrives after its store
+      mbar_init(&clink[i], 32);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -244,35 +327,35 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  if (warp >= L::WARP_TMA) {
+    regs_decrease<L::REGS_PRODUCER>();
   if (warp == L::WARP_TMA) {
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmDO);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      const int nslots = has1 ? 2 : 1;
-      mbar_arrive_expect_tx(q_full, 2 * nslots * L::QB);
-      for (int s = 0; s < nslots; ++s)
+      mbar_arrive_expect_tx(q_full, 2 * L::QB);
 #pragma unroll
-        for (int bx = 0; bx < D / 64; ++bx) {
-          tma_load_3d(sQ + s * L::QB + bx * L::QBOX, &tmQ, q_full, bx * 64, (2 * pair + s) * L::BM, bh);
-          tma_load_3d(sQ + (2 + s) * L::QB + bx * L::QBOX, &tmDO, q_full, bx * 64, (2 * pair + s) * L::BM, bh);
-        }
+      for (int bx = 0; bx < D / 64; ++bx) {
+        tma_load_3d(sQ + bx * L::KBOX, &tmQ, q_full, bx * 64, qt * L::BM, bh);
+        tma_load_3d(sDO + bx * L::KBOX, &tmDO, q_full, bx * 64, qt * L::BM, bh);
+      }
       int nk = 0, nv = 0;
       for (int n = 0; n < N; ++n) {
         const int ks = n % L::KS;
-        if (!mbar_wait_fast(&k_empty[ks], ((n / L::KS) & 1) ^ 1, g)) break;
+        if (!mbar_wait(&k_empty[ks], ((n / L::KS) & 1) ^ 1, g)) break;
         mbar_arrive_expect_tx(&k_full[ks], L::TILE);
 #pragma unroll
         for (int bx = 0; bx < D / 64; ++bx)
-          tma_load_3d(sK + ks * L::TILE + bx * L::KBOX, &tmK, &k_full[ks], bx * 64, n * L::BN, zkv);
+          tma_load_3d(sK + ks * L::TILE + bx * L::KBOX, &tmK, &k_full[ks], bx * 64, n * BN, zkv);
         ++nk;
         const int vs = n % L::VS;
-        if (!mbar_wait_fast(&v_empty[vs], ((n / L::VS) & 1) ^ 1, g)) break;
+        if (!mbar_wait(&v_empty[vs], ((n / L::VS) & 1) ^ 1, g)) break;
         mbar_arrive_expect_tx(&v_full[vs], L::TILE);
 #pragma unroll
         for (int bx = 0; bx < D / 64; ++bx)
-          tma_load_3d(sV + vs * L::TILE + bx * L::KBOX, &tmV, &v_full[vs], bx * 64, n * L::BN, zkv);
+          tma_load_3d(sV + vs * L::TILE + bx * L::KBOX, &tmV, &v_full[vs], bx * 64, n * BN, zkv);
         ++nv;
       }
       mbar_drain(q_full, 0, g.timeout_ns);
@@ -287,153 +370,226 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else if (warp == L::WARP_MMA) {
     if (lane == 0) {
-      constexpr uint32_t idS = make_idesc_f16(BF16, 128, L::BN, false, false);
+      constexpr uint32_t idS = make_idesc_f16(BF16, 128, BN, false, false);
       constexpr uint32_t idQ = make_idesc_f16(BF16, 128, D, false, true);
-      const uint32_t q_addr = smem_u32(sQ);
+      const uint32_t q_addr = smem_u32(sQ), do_addr = smem_u32(sDO);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-      int kv_waited = -1;
-      int dq_cnt[2] = {0, 0};
-      auto wait_kv = [&](int n) -> bool {
-        if (kv_waited >= n) return true;
-        kv_waited = n;
-        if (!mbar_wait(&k_full[n % L::KS], (n / L::KS) & 1, g)) return false;
-        if (!mbar_wait(&v_full[n % L::VS], (n / L::VS) & 1, g)) return false;
-        tc_fence_after();
-        return true;
-      };
-      // S_s = Q_s K_n^T and dS_s = dO_s V_n^T (64 key columns each)
-      auto issue_SdS = [&](int s, int n) -> bool {
-        if (!wait_kv(n)) return false;
-        const int ks = n % L::KS, vs = n % L::VS;
-        const uint32_t qa = q_addr + s * L::QB, da = q_addr + (2 + s) * L::QB;
-        const uint32_t base = tmem + s * L::TM_SLOT;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t qo = (kk >> 2) * L::QBOX + (kk & 3) * 32;
-          const uint32_t ko = (kk >> 2) * L::KBOX + (kk & 3) * 32;
-          umma_ss(base + L::TM_S, make_sdesc_sw128(qa + qo, 16, 1024),
-                  make_sdesc_sw128(k_addr + ks * L::TILE + ko, 16, 1024), idS, kk > 0 ? 1u : 0u);
-        }
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t qo = (kk >> 2) * L::QBOX + (kk & 3) * 32;
-          const uint32_t ko = (kk >> 2) * L::KBOX + (kk & 3) * 32;
-          umma_ss(base + L::TM_DS, make_sdesc_sw128(da + qo, 16, 1024),
-                  make_sdesc_sw128(v_addr + vs * L::TILE + ko, 16, 1024), idS, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[s]);
-        if (s == 1 || !active(1, n)) umma_commit(&v_empty[vs]);  // V_n only feeds dS
-        return true;
-      };
+      // Non-blocking issue loop.  S(n) once K(n) landed and every softmax warp
+      // copied S(n-1) out; dP(n) once V(n) landed and dP(n-1) was copied out;
+      // dQ(n) once the softmax wrote dS(n).
       bool ok = mbar_wait(q_full, 0, g);
-      for (int s = 0; ok && s < 2; ++s)
-        if (active(s, 0)) ok = issue_SdS(s, 0);
-      for (int n = 0; ok && n < N; ++n) {
-        for (int s = 0; ok && s < 2; ++s) {
-          const bool act = active(s, n);
-          if (act) {
-            if (!(ok = mbar_wait(&dp_full[s], dq_cnt[s] & 1, g))) break;
-            tc_fence_after();
-            const int ks = n % L::KS;
-            const uint32_t base = tmem + s * L::TM_SLOT;
+      if (ok) tc_fence_after();
+      int next_s = 0, next_p = 0, next_q = 0;
+      int idle = 0;
+      uint64_t t_idle = 0;
+      while (ok && next_q < N) {
+        bool progressed = false;
+        if (next_q < next_p && mbar_test(ds_full, next_q & 1)) {
+          tc_fence_after();
+          const int ks = next_q % L::KS;
 #pragma unroll
-            for (int kk = 0; kk < L::BN / 16; ++kk) {
-              // A = dP (TMEM, aliased over S), B = K_n as (N = d, K = keys): MN-major, 64-d blocks one box apart
-              const uint64_t kdesc = make_sdesc_sw128(k_addr + ks * L::TILE + kk * 16 * 128, L::KBOX, 1024);
-              umma_ts(base + L::TM_DQ, base + L::TM_S + kk * 8, kdesc, idQ, (dq_cnt[s] > 0 || kk > 0) ? 1u : 0u);
-            }
-            umma_commit(&dq_done[s]);
-            if (s == 1 || !active(1, n)) umma_commit(&k_empty[ks]);
-            ++dq_cnt[s];
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            // A = dS (TMEM, 16 keys = 8 packed columns), B = K_n as (N = d, K = keys): MN-major
+            const uint64_t kdesc = make_sdesc_sw128(k_addr + ks * L::TILE + kk * 16 * 128, L::KBOX, 1024);
+            umma_ts(tmem + L::TM_DQ, tmem + L::TM_DS + kk * 8, kdesc, idQ, (next_q > 0 || kk > 0) ? 1u : 0u);
           }
-          if (n + 1 < N && active(s, n + 1)) {
-            // S_s(n+1) overwrites the TMEM columns dP_s(n) is read from; tcgen05.mma
-            // ops issued by one thread execute in order, so no wait is needed.
-            ok = issue_SdS(s, n + 1);
+          umma_commit(dq_done);
+          umma_commit(&k_empty[ks]);
+          ++next_q;
+          progressed = true;
+        }
+        if (next_s < N && (next_s == 0 || mbar_test(s_free, (next_s - 1) & 1)) &&
+            mbar_test(&k_full[next_s % L::KS], (next_s / L::KS) & 1)) {
+          tc_fence_after();
+          const uint32_t kb = k_addr + (next_s % L::KS) * L::TILE;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t o = (kk >> 2) * L::KBOX + (kk & 3) * 32;
+            umma_ss(tmem + L::TM_S, make_sdesc_sw128(q_addr + o, 16, 1024), make_sdesc_sw128(kb + o, 16, 1024), idS,
+                    kk > 0 ? 1u : 0u);
+          }
+          umma_commit(s_full);
+          ++next_s;
+          progressed = true;
+        }
+        if (next_p < next_s && (next_p == 0 || mbar_test(dp_free, (next_p - 1) & 1)) &&
+            mbar_test(&v_full[next_p % L::VS], (next_p / L::VS) & 1)) {
+          tc_fence_after();
+          const int vs = next_p % L::VS;
+          const uint32_t vb = v_addr + vs * L::TILE;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t o = (kk >> 2) * L::KBOX + (kk & 3) * 32;
+            umma_ss(tmem + L::TM_DP, make_sdesc_sw128(do_addr + o, 16, 1024), make_sdesc_sw128(vb + o, 16, 1024),
+                    idS, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(dp_full);
+          umma_commit(&v_empty[vs]);
+          ++next_p;
+          progressed = true;
+        }
+        if (progressed) {
+          idle = 0;
+          t_idle = 0;
+        } else {
+          __nanosleep(32);
+          if (++idle == 64) {
+            idle = 0;
+            const uint64_t now = global_timer_ns();
+            if (t_idle == 0) t_idle = now;
+            if (g.aborted()) ok = false;
+            else if (now - t_idle > g.timeout_ns) {
+              g.raise(kStatusTimeout);
+              ok = false;
+            }
           }
         }
       }
       umma_commit(mma_idle);
       mbar_drain(mma_idle, 0, g.timeout_ns);
     }
-  } else if (warp < 8) {
-    const int slot = warp >> 2;
-    const int t_row = threadIdx.x & 127;
-    const int qt = 2 * pair + slot;
+  }
+  } else {
+    regs_increase<L::REGS_SOFTMAX>();
+    // ------------------------------------------------------------ softmax: 4 x 32 keys per row
+    const int wg = warp >> 2;
+    const int quarter = warp & 3;
+    const int t_row = quarter * 32 + lane;
+    const int nwg = (wg + 1) % L::NWG;  // warpgroup this one hands its running sums to
     const int row = qt * L::BM + t_row;
     const bool row_ok = row < p.Sq;
-    const uint32_t lane_base = tmem + slot * L::TM_SLOT + ((uint32_t)((warp & 3) * 32) << 16);
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
     const float slope = load_slope(p.slopes, p.slopes_dtype, h);
-    const float c_sig = -p.sm_scale * kLog2e;
+    const float c_t = 0.5f * p.sm_scale;  // sigmoid(p) = 1/2 + tanh(p / 2) / 2
     const float c_a = p.sm_scale * kLog2e;
     const float slope2 = slope * kLog2e;
     const size_t ri = (size_t)bh * p.Sq + row;
     const float lse2 = row_ok ? p.lse[ri] * kLog2e : 0.f;
-    float zs = row_ok ? p.rowsig[ri] : 0.f;
+    const float zs_row = row_ok ? p.rowsig[ri] : 0.f;  // sigmoid suffix sum from key 0 on
     const float delta = p.delta[(size_t)bh * p.sq_pad + row];
     const int lim = row_ok ? (p.causal ? min(row + 1, p.Skv) : p.Skv) : 0;
     const bool rows_partial = (qt * L::BM + L::BM > p.Sq);
-    float cacc = 0.f;
     float2* carry_row = p.carry + (size_t)bh * p.n_kb32 * p.sq_pad + row;
     bool ok = true;
-    int it = 0;
-    if (slot == 0 || has1) {
-      for (int n = 0; n < N; ++n) {
-        if (!active(slot, n)) break;  // activity is a prefix of the sweep
-        const int key0 = n * L::BN;
-        ok = mbar_wait(&s_full[slot], it & 1, g);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
+    for (int n = 0; n < N; ++n) {
+      const int key0 = n * BN + 32 * wg;  // first key of this thread's chunk
+      const bool masked = rows_partial || (key0 + 32 > p.Skv) || (p.causal && key0 + 31 > qt * L::BM);
+      if (ok) ok = mbar_wait(s_full, n & 1, g);
+      ok = __all_sync(0xffffffffu, ok);
+      uint32_t xa[32];
+      float sg[32];
+      float tot = 0.f;
+      if (ok) {
         tc_fence_after();
-        const bool masked =
-            rows_partial || (key0 + L::BN > p.Skv) || (p.causal && key0 + L::BN - 1 > qt * L::BM);
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          uint32_t sreg[32], dsreg[32];
-          tmem_ld32(lane_base + L::TM_S + c * 32, sreg);
-          tmem_ld32(lane_base + L::TM_DS + c * 32, dsreg);
-          tmem_ld_wait32(sreg);
-          tmem_ld_fence32(dsreg);
-          if (2 * n + c < p.n_kb32) carry_row[(size_t)(2 * n + c) * p.sq_pad] = make_float2(zs, cacc);
-          uint32_t dpo[16];
-          if (masked)
-            bwd_chunk<true, BF16, false>(sreg, dsreg, key0 + c * 32, lim, c_sig, c_a, slope, slope2, lse2, delta,
-                                         zs, cacc, dpo, nullptr);
-          else
-            bwd_chunk<false, BF16, false>(sreg, dsreg, key0 + c * 32, lim, c_sig, c_a, slope, slope2, lse2,
-                                          delta, zs, cacc, dpo, nullptr);
-          tmem_st16(lane_base + L::TM_S + c * 16, dpo);  // over S columns already read
+        tmem_ld32(lane_base + L::TM_S + 32 * wg, xa);
+        tmem_ld_wait32(xa);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_free);
+        tot = masked ? bwd_a_sig<true>(xa, sg, key0, lim, c_t, c_a, lse2)
+                     : bwd_a_sig<false>(xa, sg, key0, lim, c_t, c_a, lse2);
+      }
+      // sigmoid suffix sum at this chunk's first key, from the warpgroup to the left
+      // (warpgroup 0: from warpgroup 3's previous sub-tile)
+      float z0 = zs_row;
+      if (ok && (wg > 0 || n > 0)) {
+        ok = mbar_wait(&zlink[quarter * L::NWG + wg], (wg > 0 ? n : n - 1) & 1, g);
+        z0 = xs[wg * 128 + t_row];
+      }
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      if (wg + 1 < L::NWG || n + 1 < N) {
+        xs[nwg * 128 + t_row] = z0 - tot;
+        mbar_arrive(&zlink[quarter * L::NWG + nwg]);
+      }
+      float zz = z0;
+      ok = mbar_wait(dp_full, n & 1, g);
+      ok = __all_sync(0xffffffffu, ok);
+      float dtot = 0.f;
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t dpr[16];
+          tmem_ld16(lane_base + L::TM_DP + 32 * wg + 16 * hh, dpr);
+          tmem_ld_wait16(dpr);
+          if (hh == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(dp_free);
+          }
+          dtot += masked ? bwd_a_da<true>(xa + 16 * hh, sg + 16 * hh, dpr, key0 + 16 * hh, lim, slope2, delta, zz)
+                         : bwd_a_da<false>(xa + 16 * hh, sg + 16 * hh, dpr, key0 + 16 * hh, lim, slope2, delta, zz);
         }
+      }
+      // dA prefix sum before this chunk's first key, handed along the same way
+      float cc = 0.f;
+      if (ok && (wg > 0 || n > 0)) {
+        ok = mbar_wait(&clink[quarter * L::NWG + wg], (wg > 0 ? n : n - 1) & 1, g);
+        cc = xd[wg * 128 + t_row];
+      }
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      if (wg + 1 < L::NWG || n + 1 < N) {
+        xd[nwg * 128 + t_row] = cc + dtot;
+        mbar_arrive(&clink[quarter * L::NWG + nwg]);
+      }
+      const int kb32 = key0 / 32;
+      if (kb32 < p.n_kb32) carry_row[(size_t)kb32 * p.sq_pad] = make_float2(z0, cc);
+      uint32_t dso[16];
+#pragma unroll
+      for (int j2 = 0; j2 < 16; ++j2) {
+        const float2 dA = make_float2(__uint_as_float(xa[2 * j2]), __uint_as_float(xa[2 * j2 + 1]));
+        float2 c2;
+        cc += dA.x;
+        c2.x = cc;
+        cc += dA.y;
+        c2.y = cc;
+        const float2 s2 = make_float2(sg[2 * j2], sg[2 * j2 + 1]);
+        const float2 sp = __ffma2_rn(make_float2(-s2.x, -s2.y), s2, s2);           // s (1 - s)
+        const float2 m = __fmul2_rn(sp, make_float2(-slope, -slope));
+        const float2 v = __ffma2_rn(m, c2, dA);                                   // dA - slope s (1 - s) c
+        dso[j2] = pack2<BF16>(v.x, v.y);
+      }
+      // the dS columns are free once dQ(n-1) has run
+      if (n > 0) ok = mbar_wait(dq_done, (n - 1) & 1, g);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        tc_fence_after();
+        tmem_st16(lane_base + L::TM_DS + 16 * wg, dso);
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&dp_full[slot]);
-        ++it;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ds_full);
       }
-      if (ok && it > 0) {
-        ok = mbar_wait(&dq_done[slot], (it - 1) & 1, g);
-        ok = __all_sync(0xffffffffu, ok);
+    }
+    // epilogue: dQ = scale * (dS K); warpgroup w writes columns [w D/4, (w+1) D/4)
+    if (ok && N > 0) {
+      ok = mbar_wait(dq_done, (N - 1) & 1, g);
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (ok && N > 0) {
+      tc_fence_after();
+      constexpr int CW = D / L::NWG;
+      uint32_t r[CW];
+      if (CW == 32) {
+        tmem_ld32(lane_base + L::TM_DQ + wg * CW, r);
+        tmem_ld_wait32(r);
+      } else {
+        tmem_ld16(lane_base + L::TM_DQ + wg * CW, r);
+        tmem_ld_wait16(r);
       }
-      if (ok && it > 0) {
-        tc_fence_after();
-        uint8_t* dst_row = static_cast<uint8_t*>(p.dq) + ri * D * 2;
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(lane_base + L::TM_DQ + c * 32, r);
-          tmem_ld_wait32(r);
-          if (row_ok) {
-            uint4* dst = reinterpret_cast<uint4*>(dst_row + c * 64);
-            const float sc = p.sm_scale;
+      if (row_ok) {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.dq) + ri * D * 2 + wg * CW * 2);
+        const float sc = p.sm_scale;
 #pragma unroll
-            for (int v4 = 0; v4 < 4; ++v4) {
-              uint4 pk;
-              pk.x = pack2<BF16>(__uint_as_float(r[8 * v4 + 0]) * sc, __uint_as_float(r[8 * v4 + 1]) * sc);
-              pk.y = pack2<BF16>(__uint_as_float(r[8 * v4 + 2]) * sc, __uint_as_float(r[8 * v4 + 3]) * sc);
-              pk.z = pack2<BF16>(__uint_as_float(r[8 * v4 + 4]) * sc, __uint_as_float(r[8 * v4 + 5]) * sc);
-              pk.w = pack2<BF16>(__uint_as_float(r[8 * v4 + 6]) * sc, __uint_as_float(r[8 * v4 + 7]) * sc);
-              dst[v4] = pk;
-            }
-          }
+        for (int v4 = 0; v4 < CW / 8; ++v4) {
+          uint4 pk;
+          pk.x = pack2<BF16>(__uint_as_float(r[8 * v4 + 0]) * sc, __uint_as_float(r[8 * v4 + 1]) * sc);
+          pk.y = pack2<BF16>(__uint_as_float(r[8 * v4 + 2]) * sc, __uint_as_float(r[8 * v4 + 3]) * sc);
+          pk.z = pack2<BF16>(__uint_as_float(r[8 * v4 + 4]) * sc, __uint_as_float(r[8 * v4 + 5]) * sc);
+          pk.w = pack2<BF16>(__uint_as_float(r[8 * v4 + 6]) * sc, __uint_as_float(r[8 * v4 + 7]) * sc);
+          dst[v4] = pk;
         }
       }
     }
@@ -580,7 +736,7 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
         const int m = m_start + it % nM;
         const int bhq = b * p.Hq + hh;
         const int st = it % L::QS;
-        if (!mbar_wait_fast(&qdo_empty[st], ((it / L::QS) & 1) ^ 1, g)) break;
+        if (!mbar_wait(&qdo_empty[st], ((it / L::QS) & 1) ^ 1, g)) break;
         mbar_arrive_expect_tx(&qdo_full[st], 2 * L::QB);
         uint8_t* sq = sQDO + st * 2 * L::QB;
 #pragma unroll
@@ -947,7 +1103,6 @@ inline int bwd_launch_t(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigne
   p.timeout_ns = tmo;
   p.n_qtiles = (a.Sq + 127) / 128;
   p.n_kvtiles = (a.Skv + 127) / 128;
-  p.n_kb64 = (a.Skv + 63) / 64;
   p.n_kb32 = (a.Skv + 31) / 32;
   p.n_blocks = (a.Skv + BwdBLayout<D>::KB - 1) / BwdBLayout<D>::KB;
   p.sq_pad = p.n_qtiles * 128;
@@ -958,9 +1113,6 @@ inline int bwd_launch_t(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigne
   if ((rc = make_tmap(&tdo, a.dout, D, a.Sq, a.B * a.Hq, 128, BF16))) return rc;
   if ((rc = make_tmap(&tk, a.k, D, a.Skv, a.B * a.Hkv, 128, BF16))) return rc;
   if ((rc = make_tmap(&tv, a.v, D, a.Skv, a.B * a.Hkv, 128, BF16))) return rc;
-  CUtensorMap tka, tva;
-  if ((rc = make_tmap(&tka, a.k, D, a.Skv, a.B * a.Hkv, BwdALayout<D>::BN, BF16))) return rc;
-  if ((rc = make_tmap(&tva, a.v, D, a.Skv, a.B * a.Hkv, BwdALayout<D>::BN, BF16))) return rc;
   if ((rc = make_tmap(&tkb, a.k, D, a.Skv, a.B * a.Hkv, BwdBLayout<D>::KB, BF16))) return rc;
   if ((rc = make_tmap(&tvb, a.v, D, a.Skv, a.B * a.Hkv, BwdBLayout<D>::KB, BF16))) return rc;
 
@@ -968,8 +1120,8 @@ inline int bwd_launch_t(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigne
   if (phases & 1)
     coalibi_bwd_delta_kernel<D, BF16><<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(p);
   if (phases & 2)
-    coalibi_bwd_a_kernel<D, BF16><<<a.B * a.Hq * ((p.n_qtiles + 1) / 2), BwdALayout<D>::THREADS,
-                                    BwdALayout<D>::ALLOC, stream>>>(tq, tdo, tka, tva, p);
+    coalibi_bwd_a_kernel<D, BF16><<<a.B * a.Hq * p.n_qtiles, BwdALayout<D>::THREADS, BwdALayout<D>::ALLOC,
+                                    stream>>>(tq, tdo, tk, tv, p);
   if (phases & 4)
     coalibi_bwd_b_kernel<D, BF16>
         <<<a.B * a.Hkv * p.n_blocks, BwdBLayout<D>::THREADS, BwdBLayout<D>::ALLOC, stream>>>(tq, tdo, tkb, tvb, p);

@@ -232,14 +232,14 @@ __global__ void __launch_bounds__(640, 1)
       for (int n = 0; n < N; ++n) {
         const int key0 = (last - n) * L::BN;
         const int ks = n % L::KS;
-        if (!mbar_wait_fast(&k_empty[ks], ((n / L::KS) & 1) ^ 1, g)) break;
+        if (!mbar_wait(&k_empty[ks], ((n / L::KS) & 1) ^ 1, g)) break;
         mbar_arrive_expect_tx(&k_full[ks], L::TILE);
 #pragma unroll
         for (int bx = 0; bx < D / 64; ++bx)
           tma_load_3d(sK + ks * L::TILE + bx * L::BOX, &tmK, &k_full[ks], bx * 64, key0, zkv);
         ++nk;
         const int vs = n % L::VS;
-        if (!mbar_wait_fast(&v_empty[vs], ((n / L::VS) & 1) ^ 1, g)) break;
+        if (!mbar_wait(&v_empty[vs], ((n / L::VS) & 1) ^ 1, g)) break;
         mbar_arrive_expect_tx(&v_full[vs], L::TILE);
 #pragma unroll
         for (int bx = 0; bx < D / 64; ++bx)
@@ -305,7 +305,7 @@ __global__ void __launch_bounds__(640, 1)
           const bool act = active(s, n);
           if (act) {
             // P_s(n) published by the slot's softmax warps
-            if (!(ok = mbar_wait_fast(&p_full[s], pv_cnt[s] & 1, g))) break;
+            if (!(ok = mbar_wait(&p_full[s], pv_cnt[s] & 1, g))) break;
             if (!(ok = wait_v(n))) break;
             tc_fence_after();
             const int vs = n % L::VS;
@@ -361,7 +361,7 @@ __global__ void __launch_bounds__(640, 1)
       for (int n = 0; n < N; ++n) {
         if (!active(slot, n)) continue;
         const int key0 = (last - n) * L::BN;
-        ok = mbar_wait_fast(&s_full[slot], it & 1, g);
+        ok = mbar_wait(&s_full[slot], it & 1, g);
         ok = named_bar_and(pair_bar, 64, ok);  // both halves leave together on an abort
         if (!ok) break;
         tc_fence_after();

@@ -65,18 +65,6 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
 // try_wait with an explicit suspend-time hint (ns): returns within about that
 // long even if the phase has not completed, so a polling loop built on it wakes
 // promptly (the default hint can leave a thread asleep for ~1 us after the
@@ -93,8 +81,24 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parit
   return ok != 0;
 }
 
-// Bounded wait with prompt wake-up, for the waits on the critical path.
-__device__ __forceinline__ bool mbar_wait_fast(uint64_t* bar, uint32_t parity, const CtaGuard& g) {
+// Non-blocking probe (test_wait never suspends the thread, unlike try_wait).
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait until the phase with the given parity has completed, polling with a
+// 20 ns suspend hint so the thread wakes within about that long of the phase
+// completing.  Returns false (and raises the CTA abort flag) when the wait
+// exceeds the guard's timeout or another role of the CTA has already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const CtaGuard& g) {
   if (mbar_try_wait_hint(bar, parity, 20)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
@@ -109,42 +113,11 @@ __device__ __forceinline__ bool mbar_wait_fast(uint64_t* bar, uint32_t parity, c
   }
 }
 
-// Non-blocking probe (test_wait never suspends the thread, unlike try_wait).
-__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Wait until the phase with the given parity has completed.  Returns false
-// (and raises the CTA abort flag) when the wait exceeds the guard's timeout or
-// another role of the CTA has already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const CtaGuard& g) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
-  while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
-    if (g.aborted()) return false;
-    if (global_timer_ns() - t0 > g.timeout_ns) {
-      g.raise(kStatusTimeout);
-      return false;
-    }
-  }
-}
-
 // Same, but ignores the abort flag: used while unwinding to drain copies that
 // were already issued (those always complete on their own).
 __device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
   const uint64_t t0 = global_timer_ns();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait_hint(bar, parity, 20)) {
     if (global_timer_ns() - t0 > timeout_ns) return false;
   }
   return true;
