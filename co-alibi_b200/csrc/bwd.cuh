@@ -1055,6 +1055,357 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
+// 3b. pass B for D = 128: 128-key blocks, four softmax warpgroups
+//
+// One CTA per 128 keys of a kv head, so S = Q K^T and dP = dO V^T run at
+// N = 128 and every query tile loaded from L2 serves twice the keys of a
+// 64-key block.  Warpgroup w takes keys [32w, 32w+32) of every query tile; pass
+// A's carries every 32 keys make the four chunks independent (no exchange).
+// Each thread copies its S and dP columns to registers and releases them, so
+// S/dP of the next tile run while this one is in the softmax.  P and dS share
+// one 32 KB shared-memory buffer in turn: P feeds dV^T += dO^T P, then dS
+// feeds dK^T += Q^T dS (both M = D = 128, N = 128 keys).  TMEM: S [0,128),
+// dP [128,256), dV^T [256,384), dK^T [384,512) (lanes = d, columns = keys).
+// ---------------------------------------------------------------------------
+struct BwdB128Layout {
+  static constexpr int D = 128, KB = 128, NWG = 4;
+  static constexpr int QS = 2;                    // Q/dO stages
+  static constexpr int BOX = 128 * 128;           // one [128 rows][64 cols] TMA box
+  static constexpr int KTILE = KB * D * 2;        // 32 KB
+  static constexpr int QB = 128 * D * 2;          // 32 KB
+  static constexpr int PBLK = 128 * 64 * 2;       // [128 query rows][64 keys], 16 KB
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = KTILE;
+  static constexpr int OFF_QDO = 2 * KTILE;       // QS stages of (Q, dO)
+  static constexpr int OFF_PB = OFF_QDO + QS * 2 * QB;  // P, then dS, of one query tile
+  static constexpr int OFF_BAR = OFF_PB + 2 * PBLK;
+  static constexpr int NBAR = 1 + 2 * QS + 6;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int BYTES = OFF_MISC + 16;
+  static constexpr int ALLOC = BYTES + 1024;
+  static constexpr int THREADS = 128 * NWG + 128;  // + producer warpgroup (TMA, MMA, two idle warps)
+  static constexpr int WARP_TMA = 4 * NWG, WARP_MMA = 4 * NWG + 1;
+  static constexpr int REGS_SOFTMAX = 104, REGS_PRODUCER = 64;
+  static_assert(4 * REGS_SOFTMAX + REGS_PRODUCER <= 5 * 96, "register split exceeds the launch allocation");
+  static constexpr uint32_t TM_S = 0, TM_DP = 128, TM_DV = 256, TM_DK = 384, TM_COLS = 512;
+  static_assert(ALLOC <= 232448, "shared memory budget");
+};
+
+template <bool BF16>
+__global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
+    coalibi_bwd_b128_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                            const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                            const BwdParams p) {
+  using L = BwdB128Layout;
+  constexpr int D = L::D, KB = L::KB;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem + L::OFF_K;
+  uint8_t* sV = smem + L::OFF_V;
+  uint8_t* sQDO = smem + L::OFF_QDO;
+  uint8_t* sPB = smem + L::OFF_PB;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* kv_full = bars;
+  uint64_t* qdo_full = kv_full + 1;
+  uint64_t* qdo_empty = qdo_full + L::QS;
+  uint64_t* s_full = qdo_empty + L::QS;  // S and dP of the tile are in TMEM
+  uint64_t* s_free = s_full + 1;         // every softmax warp copied them out
+  uint64_t* buf_full = s_free + 1;       // use k of the P/dS buffer written (k = 2 it: P, 2 it + 1: dS)
+  uint64_t* buf_empty = buf_full + 1;    // use k consumed by its MMA
+  uint64_t* acc_done = buf_empty + 1;
+  uint64_t* mma_idle = acc_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  int hk, blk;
+  decode_block(blockIdx.x, p.B * p.Hkv, p.n_blocks, hk, blk);  // hk = b * Hkv + g
+  const int b = hk / p.Hkv;
+  const int gkv = hk - b * p.Hkv;
+  const int G = p.Hq / p.Hkv;
+  const int key0 = blk * KB;
+  const int m_start = p.causal ? key0 / 128 : 0;
+  const int nM = max(0, p.n_qtiles - m_start);
+  const int NIT = G * nM;
+  CtaGuard g{abort_flag, p.status, p.timeout_ns};
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < L::QS; ++i) {
+      mbar_init(&qdo_full[i], 1);
+      mbar_init(&qdo_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 4 * L::NWG);
+    mbar_init(buf_full, 4 * L::NWG);
+    mbar_init(buf_empty, 1);
+    mbar_init(acc_done, 1);
+    mbar_init(mma_idle, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == L::WARP_MMA) {
+    tmem_alloc(tmem_slot, L::TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp >= L::WARP_TMA) {
+    regs_decrease<L::REGS_PRODUCER>();
+  if (warp == L::WARP_TMA) {
+    if (lane == 0 && NIT > 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmDO);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(kv_full, 2 * L::KTILE);
+#pragma unroll
+      for (int bx = 0; bx < D / 64; ++bx) {
+        tma_load_3d(sK + bx * L::BOX, &tmK, kv_full, bx * 64, key0, hk);
+        tma_load_3d(sV + bx * L::BOX, &tmV, kv_full, bx * 64, key0, hk);
+      }
+      int nq = 0;
+      for (int it = 0; it < NIT; ++it) {
+        const int hh = gkv * G + it / nM;
+        const int m = m_start + it % nM;
+        const int bhq = b * p.Hq + hh;
+        const int st = it % L::QS;
+        if (!mbar_wait(&qdo_empty[st], ((it / L::QS) & 1) ^ 1, g)) break;
+        mbar_arrive_expect_tx(&qdo_full[st], 2 * L::QB);
+        uint8_t* sq = sQDO + st * 2 * L::QB;
+#pragma unroll
+        for (int bx = 0; bx < D / 64; ++bx) {
+          tma_load_3d(sq + bx * L::BOX, &tmQ, &qdo_full[st], bx * 64, m * 128, bhq);
+          tma_load_3d(sq + L::QB + bx * L::BOX, &tmDO, &qdo_full[st], bx * 64, m * 128, bhq);
+        }
+        ++nq;
+      }
+      mbar_drain(kv_full, 0, g.timeout_ns);
+      for (int s = 0; s < L::QS; ++s) {
+        const int uses = (nq > s) ? (nq - 1 - s) / L::QS + 1 : 0;
+        if (uses > 0) mbar_drain(&qdo_full[s], (uses - 1) & 1, g.timeout_ns);
+      }
+    }
+  } else if (warp == L::WARP_MMA) {
+    if (lane == 0 && NIT > 0) {
+      constexpr uint32_t idS = make_idesc_f16(BF16, 128, KB, false, false);
+      // dV^T[d][key] = dO^T[d][row] P[row][key], dK^T = Q^T dS: A MN-major (d), B MN-major (keys)
+      constexpr uint32_t idAcc = make_idesc_f16(BF16, D, KB, true, true);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      const uint32_t qdo_addr = smem_u32(sQDO), pb_addr = smem_u32(sPB);
+      bool ok = mbar_wait(kv_full, 0, g);
+      int next_sd = 0, next_u = 0;
+      int idle = 0;
+      uint64_t t_idle = 0;
+      while (ok && next_u < 2 * NIT) {
+        // consumers of the P/dS buffer first: they free the buffer and the Q/dO stage
+        if (next_u < 2 * next_sd && mbar_test(buf_full, next_u & 1)) {
+          tc_fence_after();
+          const int it = next_u >> 1;
+          const int st = it % L::QS;
+          const uint32_t qa = qdo_addr + st * 2 * L::QB;
+          const uint32_t aa = (next_u & 1) ? qa : qa + L::QB;      // Q^T for dK, dO^T for dV
+          const uint32_t acc_t = tmem + ((next_u & 1) ? L::TM_DK : L::TM_DV);
+#pragma unroll
+          for (int kk = 0; kk < 128 / 16; ++kk) {  // K = 128 query rows, 16 per MMA
+            const uint32_t ko = kk * 16 * 128;
+            umma_ss(acc_t, make_sdesc_sw128(aa + ko, L::BOX, 1024), make_sdesc_sw128(pb_addr + ko, L::PBLK, 1024),
+                    idAcc, (it > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(buf_empty);
+          if (next_u & 1) umma_commit(&qdo_empty[st]);
+          ++next_u;
+          idle = 0;
+          t_idle = 0;
+          continue;
+        }
+        if (next_sd < NIT && (next_sd == 0 || mbar_test(s_free, (next_sd - 1) & 1)) &&
+            mbar_test(&qdo_full[next_sd % L::QS], (next_sd / L::QS) & 1)) {
+          tc_fence_after();
+          const uint32_t qa = qdo_addr + (next_sd % L::QS) * 2 * L::QB, da = qa + L::QB;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t o = (kk >> 2) * L::BOX + (kk & 3) * 32;
+            umma_ss(tmem + L::TM_S, make_sdesc_sw128(qa + o, 16, 1024), make_sdesc_sw128(k_addr + o, 16, 1024), idS,
+                    kk > 0 ? 1u : 0u);
+          }
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t o = (kk >> 2) * L::BOX + (kk & 3) * 32;
+            umma_ss(tmem + L::TM_DP, make_sdesc_sw128(da + o, 16, 1024), make_sdesc_sw128(v_addr + o, 16, 1024), idS,
+                    kk > 0 ? 1u : 0u);
+          }
+          umma_commit(s_full);
+          ++next_sd;
+          idle = 0;
+          t_idle = 0;
+          continue;
+        }
+        __nanosleep(32);
+        if (++idle == 64) {
+          idle = 0;
+          const uint64_t now = global_timer_ns();
+          if (t_idle == 0) t_idle = now;
+          if (g.aborted()) ok = false;
+          else if (now - t_idle > g.timeout_ns) {
+            g.raise(kStatusTimeout);
+            ok = false;
+          }
+        }
+      }
+      if (ok) umma_commit(acc_done);
+      umma_commit(mma_idle);
+      mbar_drain(mma_idle, 0, g.timeout_ns);
+    }
+  }
+  } else {
+    regs_increase<L::REGS_SOFTMAX>();
+    const int wg = warp >> 2;
+    const int quarter = warp & 3;
+    const int t_row = quarter * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+    const float c_sig = -p.sm_scale * kLog2e;
+    const float c_a = p.sm_scale * kLog2e;
+    const int ckey0 = key0 + 32 * wg;  // this warpgroup's 32 keys
+    const int kb32 = ckey0 / 32;
+    bool ok = true;
+    struct RowIn {
+      float lse2, delta, zs, cacc;
+    };
+    // per-row inputs of an iteration, loaded one iteration ahead
+    auto load_row = [&](int it_) -> RowIn {
+      RowIn r{0.f, 0.f, 0.f, 0.f};
+      if (it_ >= NIT) return r;
+      const int hh_ = gkv * G + it_ / nM;
+      const int m_ = m_start + it_ % nM;
+      const int bhq_ = b * p.Hq + hh_;
+      const int row_ = m_ * 128 + t_row;
+      if (row_ < p.Sq) r.lse2 = p.lse[(size_t)bhq_ * p.Sq + row_] * kLog2e;
+      r.delta = p.delta[(size_t)bhq_ * p.sq_pad + row_];
+      if (kb32 < p.n_kb32) {
+        const float2 cin = p.carry[((size_t)bhq_ * p.n_kb32 + kb32) * p.sq_pad + row_];
+        r.zs = cin.x;
+        r.cacc = cin.y;
+      }
+      return r;
+    };
+    RowIn nxt = load_row(0);
+    // this thread's row in the 128B-swizzled P/dS tile: keys of block (wg >> 1), 16-byte chunks (wg & 1) * 4 + u
+    const uint32_t rsw = t_row & 7;
+    const uint32_t pb_row = (uint32_t)(wg >> 1) * L::PBLK + (t_row >> 3) * 1024 + rsw * 128;
+    for (int it = 0; it < NIT; ++it) {
+      const int hh = gkv * G + it / nM;
+      const int m = m_start + it % nM;
+      const int row = m * 128 + t_row;
+      const bool row_ok = row < p.Sq;
+      const float slope = load_slope(p.slopes, p.slopes_dtype, hh);
+      const float slope2 = slope * kLog2e;
+      const RowIn cur = nxt;
+      nxt = load_row(it + 1);
+      float zs = cur.zs, cacc = cur.cacc;
+      const int lim = row_ok ? (p.causal ? min(row + 1, p.Skv) : p.Skv) : 0;
+      const bool masked =
+          (m * 128 + 128 > p.Sq) || (ckey0 + 32 > p.Skv) || (p.causal && ckey0 + 31 > m * 128);
+      ok = mbar_wait(s_full, it & 1, g);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sreg[32], dsreg[32];
+      tmem_ld32(lane_base + L::TM_S + 32 * wg, sreg);
+      tmem_ld32(lane_base + L::TM_DP + 32 * wg, dsreg);
+      tmem_ld_wait32(sreg);
+      tmem_ld_fence32(dsreg);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free);
+      uint32_t po[16], dpo[16];
+      if (masked)
+        bwd_chunk<true, BF16, true>(sreg, dsreg, ckey0, lim, c_sig, c_a, slope, slope2, cur.lse2, cur.delta, zs,
+                                    cacc, dpo, po);
+      else
+        bwd_chunk<false, BF16, true>(sreg, dsreg, ckey0, lim, c_sig, c_a, slope, slope2, cur.lse2, cur.delta, zs,
+                                     cacc, dpo, po);
+      // use 2 it of the buffer (P) once use 2 it - 1 (dS of the previous tile) was consumed
+      if (it > 0) ok = mbar_wait(buf_empty, 1, g);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t off = pb_row + ((((uint32_t)(wg & 1) * 4 + u) ^ rsw) << 4);
+        *reinterpret_cast<uint4*>(sPB + off) = make_uint4(po[4 * u], po[4 * u + 1], po[4 * u + 2], po[4 * u + 3]);
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(buf_full);
+      // use 2 it + 1 (dS) once dV^T consumed P
+      ok = mbar_wait(buf_empty, 0, g);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t off = pb_row + ((((uint32_t)(wg & 1) * 4 + u) ^ rsw) << 4);
+        *reinterpret_cast<uint4*>(sPB + off) =
+            make_uint4(dpo[4 * u], dpo[4 * u + 1], dpo[4 * u + 2], dpo[4 * u + 3]);
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(buf_full);
+    }
+    // epilogue: lanes = d, columns = keys; warpgroup w writes its 32 keys
+    const int bkv = hk;
+    if (NIT > 0) {
+      if (ok) {
+        ok = mbar_wait(acc_done, 0, g);
+        ok = __all_sync(0xffffffffu, ok);
+      }
+      if (ok) {
+        tc_fence_after();
+        const int d = t_row;
+        uint32_t rv[32], rk[32];
+        tmem_ld32(lane_base + L::TM_DV + 32 * wg, rv);
+        tmem_ld32(lane_base + L::TM_DK + 32 * wg, rk);
+        tmem_ld_wait32(rv);
+        tmem_ld_fence32(rk);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int key = ckey0 + j;
+          if (key < p.Skv) {
+            const size_t o = ((size_t)bkv * p.Skv + key) * D + d;
+            const uint32_t pv = pack2<BF16>(__uint_as_float(rv[j]), 0.f);
+            const uint32_t pk = pack2<BF16>(__uint_as_float(rk[j]) * p.sm_scale, 0.f);
+            static_cast<uint16_t*>(p.dv)[o] = (uint16_t)(pv & 0xffffu);
+            static_cast<uint16_t*>(p.dk)[o] = (uint16_t)(pk & 0xffffu);
+          }
+        }
+      }
+    } else {
+      // no query row sees these keys: their gradients are zero
+      const int d = t_row;
+      for (int j = 0; j < 32; ++j) {
+        const int key = ckey0 + j;
+        if (key < p.Skv) {
+          const size_t o = ((size_t)bkv * p.Skv + key) * D + d;
+          static_cast<uint16_t*>(p.dv)[o] = 0;
+          static_cast<uint16_t*>(p.dk)[o] = 0;
+        }
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == L::WARP_MMA) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host-side helpers (called from coalibi.cu)
 // ---------------------------------------------------------------------------
 int make_tmap(CUtensorMap* map, const void* base, int D, int rows, int heads, int box_rows, bool bf16);
@@ -1070,8 +1421,8 @@ inline bool bwd_set_smem_attributes() {
   ok &= bwd_set_smem_one(coalibi_bwd_a_kernel<128, true>, BwdALayout<128>::ALLOC);
   ok &= bwd_set_smem_one(coalibi_bwd_a_kernel<64, false>, BwdALayout<64>::ALLOC);
   ok &= bwd_set_smem_one(coalibi_bwd_a_kernel<64, true>, BwdALayout<64>::ALLOC);
-  ok &= bwd_set_smem_one(coalibi_bwd_b_kernel<128, false>, BwdBLayout<128>::ALLOC);
-  ok &= bwd_set_smem_one(coalibi_bwd_b_kernel<128, true>, BwdBLayout<128>::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_b128_kernel<false>, BwdB128Layout::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_b128_kernel<true>, BwdB128Layout::ALLOC);
   ok &= bwd_set_smem_one(coalibi_bwd_b_kernel<64, false>, BwdBLayout<64>::ALLOC);
   ok &= bwd_set_smem_one(coalibi_bwd_b_kernel<64, true>, BwdBLayout<64>::ALLOC);
   return ok;
@@ -1104,7 +1455,8 @@ inline int bwd_launch_t(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigne
   p.n_qtiles = (a.Sq + 127) / 128;
   p.n_kvtiles = (a.Skv + 127) / 128;
   p.n_kb32 = (a.Skv + 31) / 32;
-  p.n_blocks = (a.Skv + BwdBLayout<D>::KB - 1) / BwdBLayout<D>::KB;
+  const int kb_b = (D == 128) ? BwdB128Layout::KB : BwdBLayout<D>::KB;
+  p.n_blocks = (a.Skv + kb_b - 1) / kb_b;
   p.sq_pad = p.n_qtiles * 128;
 
   CUtensorMap tq, tdo, tk, tv, tkb, tvb;
@@ -1113,8 +1465,8 @@ inline int bwd_launch_t(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigne
   if ((rc = make_tmap(&tdo, a.dout, D, a.Sq, a.B * a.Hq, 128, BF16))) return rc;
   if ((rc = make_tmap(&tk, a.k, D, a.Skv, a.B * a.Hkv, 128, BF16))) return rc;
   if ((rc = make_tmap(&tv, a.v, D, a.Skv, a.B * a.Hkv, 128, BF16))) return rc;
-  if ((rc = make_tmap(&tkb, a.k, D, a.Skv, a.B * a.Hkv, BwdBLayout<D>::KB, BF16))) return rc;
-  if ((rc = make_tmap(&tvb, a.v, D, a.Skv, a.B * a.Hkv, BwdBLayout<D>::KB, BF16))) return rc;
+  if ((rc = make_tmap(&tkb, a.k, D, a.Skv, a.B * a.Hkv, kb_b, BF16))) return rc;
+  if ((rc = make_tmap(&tvb, a.v, D, a.Skv, a.B * a.Hkv, kb_b, BF16))) return rc;
 
   const long long rows = (long long)a.B * a.Hq * p.sq_pad;
   if (phases & 1)
@@ -1122,9 +1474,14 @@ inline int bwd_launch_t(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigne
   if (phases & 2)
     coalibi_bwd_a_kernel<D, BF16><<<a.B * a.Hq * p.n_qtiles, BwdALayout<D>::THREADS, BwdALayout<D>::ALLOC,
                                     stream>>>(tq, tdo, tk, tv, p);
-  if (phases & 4)
-    coalibi_bwd_b_kernel<D, BF16>
-        <<<a.B * a.Hkv * p.n_blocks, BwdBLayout<D>::THREADS, BwdBLayout<D>::ALLOC, stream>>>(tq, tdo, tkb, tvb, p);
+  if (phases & 4) {
+    if constexpr (D == 128)
+      coalibi_bwd_b128_kernel<BF16>
+          <<<a.B * a.Hkv * p.n_blocks, BwdB128Layout::THREADS, BwdB128Layout::ALLOC, stream>>>(tq, tdo, tkb, tvb, p);
+    else
+      coalibi_bwd_b_kernel<D, BF16>
+          <<<a.B * a.Hkv * p.n_blocks, BwdBLayout<D>::THREADS, BwdBLayout<D>::ALLOC, stream>>>(tq, tdo, tkb, tvb, p);
+  }
   return cudaGetLastError() == cudaSuccess ? COALIBI_OK : COALIBI_ERR_LAUNCH;
 }
 
