@@ -109,39 +109,45 @@ __global__ void __launch_bounds__(256) coalibi_bwd_delta_kernel(const BwdParams 
 }
 
 // ---------------------------------------------------------------------------
-// Shared per-key maths of passes A and B: one 32-key chunk of a row, keys left
+// Per-key maths of pass B: one 32-key chunk of a row, keys left
 // to right.  zs = suffix sum of sigmoids from the current key on (inclusive),
 // cacc = inclusive prefix of dA.  Writes 16 packed dp pairs and, if P_OUT, 16
 // packed P pairs.  Keys >= lim are masked.
 // ---------------------------------------------------------------------------
 template <bool MASK, bool BF16, bool P_OUT>
 __device__ __forceinline__ void bwd_chunk(const uint32_t* sreg, const uint32_t* dsreg, int key0, int lim,
-                                          float c_sig, float c_a, float slope, float slope2, float lse2,
+                                          float c_t, float c_a, float slope, float slope2, float lse2,
                                           float delta, float& zs, float& cacc, uint32_t* dp_out,
                                           uint32_t* p_out) {
+  // two keys per packed f32x2 instruction; sigmoid(p) = 1/2 + tanh(p / 2) / 2
 #pragma unroll
   for (int j2 = 0; j2 < 16; ++j2) {
-    float dpv[2], pv[2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int j = 2 * j2 + u;
-      const float x = __uint_as_float(sreg[j]);
-      const float y = __uint_as_float(dsreg[j]);
-      float sg = sigmoid_from_neg_log2(x * c_sig);
-      const bool valid = !MASK || (key0 + j < lim);
-      if (!valid) sg = 0.f;
-      const float a2 = fmaf(-slope2, zs, x * c_a);
-      float P = ex2_approx(a2 - lse2);
-      if (!valid) P = 0.f;
-      const float dA = P * (y - delta);
-      cacc += dA;
-      const float sp = fmaf(-sg, sg, sg);  // s (1 - s)
-      dpv[u] = fmaf(-slope * sp, cacc, dA);
-      pv[u] = P;
-      zs -= sg;
-    }
-    dp_out[j2] = pack2<BF16>(dpv[0], dpv[1]);
-    if (P_OUT) p_out[j2] = pack2<BF16>(pv[0], pv[1]);
+    const int j = 2 * j2;
+    const float2 x = make_float2(__uint_as_float(sreg[j]), __uint_as_float(sreg[j + 1]));
+    const float2 y = make_float2(__uint_as_float(dsreg[j]), __uint_as_float(dsreg[j + 1]));
+    const float2 u = __fmul2_rn(x, make_float2(c_t, c_t));
+    float2 sg = __ffma2_rn(make_float2(0.5f, 0.5f), make_float2(tanh_approx(u.x), tanh_approx(u.y)),
+                           make_float2(0.5f, 0.5f));
+    if (MASK && key0 + j >= lim) sg.x = 0.f;
+    if (MASK && key0 + j + 1 >= lim) sg.y = 0.f;
+    float2 z;  // sigmoid suffix from each key on (inclusive)
+    z.x = zs;
+    z.y = zs - sg.x;
+    zs = z.y - sg.y;
+    const float2 e = __ffma2_rn(make_float2(-slope2, -slope2), z,
+                                __ffma2_rn(x, make_float2(c_a, c_a), make_float2(-lse2, -lse2)));
+    float2 P = make_float2(ex2_approx(e.x), ex2_approx(e.y));
+    if (MASK && key0 + j >= lim) P.x = 0.f;
+    if (MASK && key0 + j + 1 >= lim) P.y = 0.f;
+    const float2 dA = __fmul2_rn(P, __fadd2_rn(y, make_float2(-delta, -delta)));
+    float2 c;  // dA prefix up to each key (inclusive)
+    c.x = cacc + dA.x;
+    c.y = c.x + dA.y;
+    cacc = c.y;
+    const float2 sp = __ffma2_rn(make_float2(-sg.x, -sg.y), sg, sg);  // s (1 - s)
+    const float2 dp = __ffma2_rn(__fmul2_rn(sp, make_float2(-slope, -slope)), c, dA);
+    dp_out[j2] = pack2<BF16>(dp.x, dp.y);
+    if (P_OUT) p_out[j2] = pack2<BF16>(P.x, P.y);
   }
 }
 
@@ -863,7 +869,7 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
     const int wg = warp >> 2;
     const int t_row = threadIdx.x & 127;
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    const float c_sig = -p.sm_scale * kLog2e;
+    const float c_t = 0.5f * p.sm_scale;
     const float c_a = p.sm_scale * kLog2e;
     // keys of the block this thread covers: [key0 + wkey0, key0 + wkey0 + WKB)
     constexpr int WKB = KB / L::NWG;
@@ -933,10 +939,10 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
         }
         uint32_t po[16], dpo[16];
         if (masked)
-          bwd_chunk<true, BF16, true>(sreg, dsreg, key0 + kc * 32, lim, c_sig, c_a, slope, slope2, lse2, delta,
+          bwd_chunk<true, BF16, true>(sreg, dsreg, key0 + kc * 32, lim, c_t, c_a, slope, slope2, lse2, delta,
                                       zs, cacc, dpo, po);
         else
-          bwd_chunk<false, BF16, true>(sreg, dsreg, key0 + kc * 32, lim, c_sig, c_a, slope, slope2, lse2, delta,
+          bwd_chunk<false, BF16, true>(sreg, dsreg, key0 + kc * 32, lim, c_t, c_a, slope, slope2, lse2, delta,
                                        zs, cacc, dpo, po);
         // 32 keys = four 16-byte chunks; 64-key swizzle rows, 128x128-byte blocks
 #pragma unroll
@@ -1268,7 +1274,7 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
     const int quarter = warp & 3;
     const int t_row = quarter * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
-    const float c_sig = -p.sm_scale * kLog2e;
+    const float c_t = 0.5f * p.sm_scale;
     const float c_a = p.sm_scale * kLog2e;
     const int ckey0 = key0 + 32 * wg;  // this warpgroup's 32 keys
     const int kb32 = ckey0 / 32;
@@ -1276,7 +1282,8 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
     struct RowIn {
       float lse2, delta, zs, cacc;
     };
-    // per-row inputs of an iteration, loaded one iteration ahead
+    // per-row inputs of an iteration, loaded one iteration ahead (pinned loads: the
+    // compiler would otherwise sink them next to their use and expose the latency)
     auto load_row = [&](int it_) -> RowIn {
       RowIn r{0.f, 0.f, 0.f, 0.f};
       if (it_ >= NIT) return r;
@@ -1284,15 +1291,17 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
       const int m_ = m_start + it_ % nM;
       const int bhq_ = b * p.Hq + hh_;
       const int row_ = m_ * 128 + t_row;
-      if (row_ < p.Sq) r.lse2 = p.lse[(size_t)bhq_ * p.Sq + row_] * kLog2e;
-      r.delta = p.delta[(size_t)bhq_ * p.sq_pad + row_];
+      if (row_ < p.Sq) r.lse2 = ldg_pinned(p.lse + (size_t)bhq_ * p.Sq + row_);
+      r.delta = ldg_pinned(p.delta + (size_t)bhq_ * p.sq_pad + row_);
       if (kb32 < p.n_kb32) {
-        const float2 cin = p.carry[((size_t)bhq_ * p.n_kb32 + kb32) * p.sq_pad + row_];
+        const float2 cin = ldg_pinned(p.carry + ((size_t)bhq_ * p.n_kb32 + kb32) * p.sq_pad + row_);
         r.zs = cin.x;
         r.cacc = cin.y;
       }
       return r;
     };
+    int slope_hh = -1;
+    float slope = 0.f;
     RowIn nxt = load_row(0);
     // this thread's row in the 128B-swizzled P/dS tile: keys of block (wg >> 1), 16-byte chunks (wg & 1) * 4 + u
     const uint32_t rsw = t_row & 7;
@@ -1302,7 +1311,10 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
       const int m = m_start + it % nM;
       const int row = m * 128 + t_row;
       const bool row_ok = row < p.Sq;
-      const float slope = load_slope(p.slopes, p.slopes_dtype, hh);
+      if (hh != slope_hh) {
+        slope = load_slope(p.slopes, p.slopes_dtype, hh);
+        slope_hh = hh;
+      }
       const float slope2 = slope * kLog2e;
       const RowIn cur = nxt;
       nxt = load_row(it + 1);
@@ -1324,11 +1336,11 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
       if (lane == 0) mbar_arrive(s_free);
       uint32_t po[16], dpo[16];
       if (masked)
-        bwd_chunk<true, BF16, true>(sreg, dsreg, ckey0, lim, c_sig, c_a, slope, slope2, cur.lse2, cur.delta, zs,
-                                    cacc, dpo, po);
+        bwd_chunk<true, BF16, true>(sreg, dsreg, ckey0, lim, c_t, c_a, slope, slope2, cur.lse2 * kLog2e,
+                                    cur.delta, zs, cacc, dpo, po);
       else
-        bwd_chunk<false, BF16, true>(sreg, dsreg, ckey0, lim, c_sig, c_a, slope, slope2, cur.lse2, cur.delta, zs,
-                                     cacc, dpo, po);
+        bwd_chunk<false, BF16, true>(sreg, dsreg, ckey0, lim, c_t, c_a, slope, slope2, cur.lse2 * kLog2e,
+                                     cur.delta, zs, cacc, dpo, po);
       // use 2 it of the buffer (P) once use 2 it - 1 (dS of the previous tile) was consumed
       if (it > 0) ok = mbar_wait(buf_empty, 1, g);
       ok = __all_sync(0xffffffffu, ok);

@@ -322,6 +322,21 @@ __device__ __forceinline__ void regs_decrease() {
 }
 
 // ----------------------------------------------------------------------------
+// Read-only global loads the compiler may not move: a prefetch issued early in
+// a loop body stays there instead of sinking to its first use.
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ float ldg_pinned(const float* p) {
+  float v;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float2 ldg_pinned(const float2* p) {
+  float2 v;
+  asm volatile("ld.global.nc.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "l"(p));
+  return v;
+}
+
+// ----------------------------------------------------------------------------
 // Scalar helpers
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ float ex2_approx(float x) {
