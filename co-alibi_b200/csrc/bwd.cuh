@@ -1207,24 +1207,29 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
       int next_sd = 0, next_u = 0;
       int idle = 0;
       uint64_t t_idle = 0;
-      while (ok && next_u < 2 * NIT) {
-        // consumers of the P/dS buffer first: they free the buffer and the Q/dO stage
-        if (next_u < 2 * next_sd && mbar_test(buf_full, next_u & 1)) {
-          tc_fence_after();
-          const int it = next_u >> 1;
-          const int st = it % L::QS;
-          const uint32_t qa = qdo_addr + st * 2 * L::QB;
-          const uint32_t aa = (next_u & 1) ? qa : qa + L::QB;      // Q^T for dK, dO^T for dV
-          const uint32_t acc_t = tmem + ((next_u & 1) ? L::TM_DK : L::TM_DV);
+      // consumer of the P/dS buffer (dV^T for P, dK^T for dS): it frees the buffer
+      // for the softmax and, after dK^T, the Q/dO stage
+      auto try_consume = [&]() -> bool {
+        if (!(next_u < 2 * next_sd && mbar_test(buf_full, next_u & 1))) return false;
+        tc_fence_after();
+        const int it = next_u >> 1;
+        const int st = it % L::QS;
+        const uint32_t qa = qdo_addr + st * 2 * L::QB;
+        const uint32_t aa = (next_u & 1) ? qa : qa + L::QB;      // Q^T for dK, dO^T for dV
+        const uint32_t acc_t = tmem + ((next_u & 1) ? L::TM_DK : L::TM_DV);
 #pragma unroll
-          for (int kk = 0; kk < 128 / 16; ++kk) {  // K = 128 query rows, 16 per MMA
-            const uint32_t ko = kk * 16 * 128;
-            umma_ss(acc_t, make_sdesc_sw128(aa + ko, L::BOX, 1024), make_sdesc_sw128(pb_addr + ko, L::PBLK, 1024),
-                    idAcc, (it > 0 || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(buf_empty);
-          if (next_u & 1) umma_commit(&qdo_empty[st]);
-          ++next_u;
+        for (int kk = 0; kk < 128 / 16; ++kk) {  // K = 128 query rows, 16 per MMA
+          const uint32_t ko = kk * 16 * 128;
+          umma_ss(acc_t, make_sdesc_sw128(aa + ko, L::BOX, 1024), make_sdesc_sw128(pb_addr + ko, L::PBLK, 1024),
+                  idAcc, (it > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(buf_empty);
+        if (next_u & 1) umma_commit(&qdo_empty[st]);
+        ++next_u;
+        return true;
+      };
+      while (ok && next_u < 2 * NIT) {
+        if (try_consume()) {
           idle = 0;
           t_idle = 0;
           continue;
@@ -1239,6 +1244,9 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
             umma_ss(tmem + L::TM_S, make_sdesc_sw128(qa + o, 16, 1024), make_sdesc_sw128(k_addr + o, 16, 1024), idS,
                     kk > 0 ? 1u : 0u);
           }
+          // the MMA thread blocks while the pipe drains what it issued: give a
+          // waiting buffer consumer its turn between the two halves
+          try_consume();
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t o = (kk >> 2) * L::BOX + (kk & 3) * 32;
@@ -1284,11 +1292,9 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
     };
     // per-row inputs of an iteration, loaded one iteration ahead (pinned loads: the
     // compiler would otherwise sink them next to their use and expose the latency)
-    auto load_row = [&](int it_) -> RowIn {
+    auto load_row = [&](int it_, int hh_, int m_) -> RowIn {
       RowIn r{0.f, 0.f, 0.f, 0.f};
       if (it_ >= NIT) return r;
-      const int hh_ = gkv * G + it_ / nM;
-      const int m_ = m_start + it_ % nM;
       const int bhq_ = b * p.Hq + hh_;
       const int row_ = m_ * 128 + t_row;
       if (row_ < p.Sq) r.lse2 = ldg_pinned(p.lse + (size_t)bhq_ * p.Sq + row_);
@@ -1302,13 +1308,13 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
     };
     int slope_hh = -1;
     float slope = 0.f;
-    RowIn nxt = load_row(0);
+    RowIn nxt = load_row(0, gkv * G, m_start);
+    int hh = gkv * G, m = m_start;          // head and query tile of iteration it
+    int hh_n = hh + (nM == 1 ? 1 : 0), m_n = (nM == 1) ? m_start : m_start + 1;  // of it + 1
     // this thread's row in the 128B-swizzled P/dS tile: keys of block (wg >> 1), 16-byte chunks (wg & 1) * 4 + u
     const uint32_t rsw = t_row & 7;
     const uint32_t pb_row = (uint32_t)(wg >> 1) * L::PBLK + (t_row >> 3) * 1024 + rsw * 128;
     for (int it = 0; it < NIT; ++it) {
-      const int hh = gkv * G + it / nM;
-      const int m = m_start + it % nM;
       const int row = m * 128 + t_row;
       const bool row_ok = row < p.Sq;
       if (hh != slope_hh) {
@@ -1317,7 +1323,7 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
       }
       const float slope2 = slope * kLog2e;
       const RowIn cur = nxt;
-      nxt = load_row(it + 1);
+      nxt = load_row(it + 1, hh_n, m_n);
       float zs = cur.zs, cacc = cur.cacc;
       const int lim = row_ok ? (p.causal ? min(row + 1, p.Skv) : p.Skv) : 0;
       const bool masked =
@@ -1366,6 +1372,12 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(buf_full);
+      hh = hh_n;
+      m = m_n;
+      if (++m_n == p.n_qtiles) {
+        m_n = m_start;
+        ++hh_n;
+      }
     }
     // epilogue: lanes = d, columns = keys; warpgroup w writes its 32 keys
     const int bkv = hk;
