@@ -44,7 +44,7 @@ CONFIGS = {
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of each
 # kernel at cfg2: one ncu capture at B=2 (profiles/<kernel>_kernel_cfg2_b2_ncu_full.txt)
 # scaled by 4 to the B=8 launch (traffic grows with the number of (b, h) units).
-NCU_TRAFFIC_CFG2 = {"fwd": 4 * 114.8e6, "bwd_a": 4 * 202.6e6, "bwd_b": 4 * 254.2e6, "bwd_delta": None}
+NCU_TRAFFIC_CFG2 = {"fwd": 4 * 115.7e6, "bwd_a": 4 * 209.8e6, "bwd_b": 4 * 251.2e6, "bwd_delta": None}
 
 
 def visible(S, causal):

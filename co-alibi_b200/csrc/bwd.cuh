@@ -11,20 +11,21 @@
 // key-major kernel cannot form them on its own.  The split is:
 //
 //  1. delta pre-pass: delta_i = dO_i . O_i (one warp per row).
-//  2. pass A, query-major (one CTA per 128-row query tile, key tiles left to
-//     right): recomputes S = Q K^T and dS = dO V^T into TMEM, runs the two
-//     scans in registers (one thread per row), accumulates dQ += dp K in TMEM,
-//     and records at every 64-key boundary the pair (z suffix, c prefix) of
-//     each row -- 8 bytes per (row, 64 keys).
+//  2. pass A, query-major (one CTA per 128-row query tile, 128-key sub-tiles
+//     left to right): recomputes S = Q K^T and dP = dO V^T into TMEM, runs the
+//     two scans (four warpgroups of 32 keys, running sums handed along the
+//     row), accumulates dQ += dS K in TMEM, and records at every 32-key
+//     boundary the pair (z suffix, c prefix) of each row -- 8 bytes per
+//     (row, 32 keys).
 //  3. pass B, key-major (one CTA per block of keys of one kv head): for every
 //     query head of the GQA group and every query tile that sees the block it
-//     recomputes S and dS, restarts both scans from pass A's carries, writes
-//     P and dp to shared memory and accumulates dV += P^T dO and dK += dp^T Q
+//     recomputes S and dP, restarts both scans from pass A's carries, writes
+//     P and dS to shared memory and accumulates dV += P^T dO and dK += dS^T Q
 //     in TMEM.  The GQA group sum therefore happens in TMEM.
 //
-// D = 128 uses 64-key blocks in pass B with transposed accumulators
-// (dV^T = dO^T P, M = D); D = 64 uses 128-key blocks (dV = P^T dO, M = keys).
-// Both keep every MMA at M = 128.
+// D = 128 uses 128-key blocks in pass B with four warpgroups and transposed
+// accumulators (dV^T = dO^T P, M = D); D = 64 uses 128-key blocks with one
+// warpgroup (dV = P^T dO, M = keys).  Every MMA has M = 128.
 #pragma once
 
 #include <cuda.h>
