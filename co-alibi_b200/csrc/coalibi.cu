@@ -69,6 +69,7 @@ constexpr unsigned kDefaultTimeoutMs = 2000;
 struct DeviceState {
   std::once_flag once;
   int status = COALIBI_ERR_DEVICE;
+  int sm_count = 0;
 };
 DeviceState g_dev[kMaxDevices];
 
@@ -112,6 +113,11 @@ int device_setup(const void* ptr) {
       st.status = COALIBI_ERR_DEVICE;
       return;
     }
+    if (cudaDeviceGetAttribute(&st.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        st.sm_count <= 0) {
+      st.status = COALIBI_ERR_DEVICE;
+      return;
+    }
     bool ok = true;
     ok &= set_smem(coalibi_fwd_kernel<128, false>, FwdLayout<128>::ALLOC);
     ok &= set_smem(coalibi_fwd_kernel<128, true>, FwdLayout<128>::ALLOC);
@@ -121,6 +127,13 @@ int device_setup(const void* ptr) {
     st.status = ok ? COALIBI_OK : COALIBI_ERR_LAUNCH;
   });
   return st.status;
+}
+
+// SM count of the current device (device_setup has run for it)
+int current_sm_count() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return g_dev[dev].sm_count;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -145,7 +158,9 @@ unsigned long long timeout_ns(unsigned ms) {
 template <int D, bool BF16>
 int launch_fwd_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const FwdParams& p,
                cudaStream_t stream) {
-  const int grid = p.B * p.Hq * ((p.n_qtiles + 1) / 2);
+  // persistent: one CTA per SM walks (head, query tile) items in a static round robin
+  const int n_items = p.B * p.Hq * p.n_qtiles;
+  const int grid = n_items < current_sm_count() ? n_items : current_sm_count();
   coalibi_fwd_kernel<D, BF16><<<grid, FwdLayout<D>::THREADS, FwdLayout<D>::ALLOC, stream>>>(tq, tk, tv, p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
