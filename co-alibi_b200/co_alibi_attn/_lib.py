@@ -40,7 +40,8 @@ class CoalibiBwdArgs(ctypes.Structure):
 
 
 EXPORTS = ("coalibi_fwd", "coalibi_bwd", "coalibi_bwd_phases", "coalibi_bwd_noalloc",
-           "coalibi_bwd_workspace_bytes", "coalibi_strerror", "coalibi_abi_version", "coalibi_last_error")
+           "coalibi_bwd_workspace_bytes", "coalibi_selftest_wait_timeout", "coalibi_strerror",
+           "coalibi_abi_version", "coalibi_last_error")
 
 NOALLOC_SCRATCH_BYTES = 64 << 20  # COALIBI_NOALLOC_SCRATCH_BYTES
 
@@ -70,6 +71,8 @@ def load():
             lib.coalibi_bwd_noalloc.restype = c_int
             lib.coalibi_bwd_workspace_bytes.argtypes = [c_int] * 6
             lib.coalibi_bwd_workspace_bytes.restype = c_size_t
+            lib.coalibi_selftest_wait_timeout.argtypes = [ctypes.c_uint, c_void_p, c_void_p]
+            lib.coalibi_selftest_wait_timeout.restype = c_int
             lib.coalibi_strerror.argtypes = [c_int]
             lib.coalibi_strerror.restype = ctypes.c_char_p
             lib.coalibi_last_error.argtypes = []

@@ -179,7 +179,39 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
 }  // namespace
 }  // namespace coalibi
 
+namespace coalibi {
+namespace {
+// Warps wait on barriers nothing arrives on: the first to time out raises the
+// abort flag and the status word; the others see the flag and return too.
+__global__ void __launch_bounds__(64) selftest_wait_kernel(int* status, unsigned long long timeout_ns) {
+  __shared__ uint64_t bar[2];
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  CtaGuard g{&abort_flag, status, timeout_ns};
+  mbar_wait(&bar[threadIdx.x >> 5], 0, g);
+}
+}  // namespace
+}  // namespace coalibi
+
 using namespace coalibi;
+
+extern "C" int coalibi_selftest_wait_timeout(unsigned int timeout_ms, int* status, void* stream) {
+  if (status == nullptr) return COALIBI_ERR_NULL_POINTER;
+  if (int rc = device_setup(status)) return rc;
+  selftest_wait_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(status, timeout_ns(timeout_ms));
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    snprintf(g_last_error, sizeof(g_last_error), "self-test launch: %s", cudaGetErrorString(e));
+    return COALIBI_ERR_LAUNCH;
+  }
+  return COALIBI_OK;
+}
 
 extern "C" int coalibi_fwd(const CoalibiFwdArgs* a, void* stream) {
   if (a == nullptr) return COALIBI_ERR_NULL_POINTER;

@@ -110,7 +110,7 @@ int coalibi_bwd(const CoalibiBwdArgs* args, void* stream);
 
 /* Profiling aid with no counterpart in the reference: launch only the backward
  * kernels selected by phase_mask (bit 0: delta = rowsum(dO * O) pre-pass, bit 1:
- * pass A -> dq and the per-64-key carries in the workspace, bit 2: pass B -> dk, dv).
+ * pass A -> dq and the per-32-key carries in the workspace, bit 2: pass B -> dk, dv).
  * Phases read what earlier phases wrote into the workspace, so they must run in
  * order on one stream; coalibi_bwd(args, s) == coalibi_bwd_phases(args, 7, s). */
 int coalibi_bwd_phases(const CoalibiBwdArgs* args, int phase_mask, void* stream);
@@ -130,6 +130,15 @@ int coalibi_bwd_phases(const CoalibiBwdArgs* args, int phase_mask, void* stream)
  * address (cudaGetSymbolAddress); make it before any stream capture.  All calls on
  * a device share the array, so calls that overlap on the GPU race: serialise them. */
 int coalibi_bwd_noalloc(const CoalibiBwdArgs* args, void* stream);
+
+/* Self-test of the kernels' bounded waits, with no counterpart in the reference:
+ * enqueues one CTA whose warps wait on mbarriers that nothing ever arrives on.
+ * Every such wait in this library gives up after its timeout, raises the CTA's
+ * abort flag and records COALIBI_ERR_TIMEOUT in the device word *status (if it
+ * still holds 0), so the kernel ends after about timeout_ms (0: the default of
+ * 2000) and the CUDA context stays usable.  Returns the launch result; read
+ * *status after synchronising the stream. */
+int coalibi_selftest_wait_timeout(unsigned int timeout_ms, int* status, void* stream);
 
 /* Static name of an error code. */
 const char* coalibi_strerror(int code);
