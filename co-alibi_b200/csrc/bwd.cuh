@@ -10,7 +10,7 @@
 // z and c are running sums along the key axis of each query row, so a
 // key-major kernel cannot form them on its own.  The split is:
 //
-//  1. delta pre-pass: delta_i = dO_i . O_i (one warp per row).
+//  1. delta pre-pass: delta_i = dO_i . O_i (16-byte loads, D/8 lanes per row).
 //  2. pass A, query-major (one CTA per 128-row query tile, 128-key sub-tiles
 //     left to right): recomputes S = Q K^T and dP = dO V^T into TMEM, runs the
 //     two scans (four warpgroups of 32 keys, running sums handed along the
@@ -82,31 +82,33 @@ struct BwdParams {
 // ---------------------------------------------------------------------------
 template <int D, bool BF16>
 __global__ void __launch_bounds__(256) coalibi_bwd_delta_kernel(const BwdParams p) {
+  // 16-byte loads: D / 8 lanes per row, 32 / (D / 8) rows per warp
+  constexpr int LPR = D / 8;
+  constexpr int RPW = 32 / LPR;
   const long long nrows = (long long)p.B * p.Hq * p.sq_pad;
-  const long long rg = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (rg >= nrows) return;
   const int lane = threadIdx.x & 31;
-  const int bh = (int)(rg / p.sq_pad);
-  const int row = (int)(rg - (long long)bh * p.sq_pad);
+  const long long rg = ((long long)blockIdx.x * 8 + (threadIdx.x >> 5)) * RPW + lane / LPR;
+  const int sub = lane % LPR;
   float acc = 0.f;
-  if (row < p.Sq) {
-    const size_t base = ((size_t)bh * p.Sq + row) * D;
-    if (D == 128) {
-      const uint2 a = reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.o) + base)[lane];
-      const uint2 b = reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.dout) + base)[lane];
-      const float2 a0 = unpack2<BF16>(a.x), a1 = unpack2<BF16>(a.y);
-      const float2 b0 = unpack2<BF16>(b.x), b1 = unpack2<BF16>(b.y);
-      acc = a0.x * b0.x + a0.y * b0.y + a1.x * b1.x + a1.y * b1.y;
-    } else {
-      const uint32_t a = reinterpret_cast<const uint32_t*>(static_cast<const uint16_t*>(p.o) + base)[lane];
-      const uint32_t b = reinterpret_cast<const uint32_t*>(static_cast<const uint16_t*>(p.dout) + base)[lane];
-      const float2 a0 = unpack2<BF16>(a), b0 = unpack2<BF16>(b);
-      acc = a0.x * b0.x + a0.y * b0.y;
+  int bh = 0, row = 0;
+  if (rg < nrows) {
+    bh = (int)(rg / p.sq_pad);
+    row = (int)(rg - (long long)bh * p.sq_pad);
+    if (row < p.Sq) {
+      const size_t base = ((size_t)bh * p.Sq + row) * D;
+      const uint4 a = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.o) + base)[sub];
+      const uint4 b = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.dout) + base)[sub];
+      const uint32_t av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 x = unpack2<BF16>(av[i]), y = unpack2<BF16>(bv[i]);
+        acc = fmaf(x.x, y.x, fmaf(x.y, y.y, acc));
+      }
     }
   }
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (lane == 0) p.delta[rg] = acc;
+  for (int off = LPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (sub == 0 && rg < nrows) p.delta[rg] = acc;
 }
 
 // ---------------------------------------------------------------------------
@@ -439,7 +441,6 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
           idle = 0;
           t_idle = 0;
         } else {
-          __nanosleep(32);
           if (++idle == 64) {
             idle = 0;
             const uint64_t now = global_timer_ns();
@@ -849,7 +850,6 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
           idle = 0;
           t_idle = 0;
         } else {
-          __nanosleep(32);
           if (++idle == 64) {
             idle = 0;
             const uint64_t now = global_timer_ns();
@@ -1260,7 +1260,6 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
           t_idle = 0;
           continue;
         }
-        __nanosleep(32);
         if (++idle == 64) {
           idle = 0;
           const uint64_t now = global_timer_ns();
@@ -1495,7 +1494,7 @@ inline int bwd_launch_t(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigne
 
   const long long rows = (long long)a.B * a.Hq * p.sq_pad;
   if (phases & 1)
-    coalibi_bwd_delta_kernel<D, BF16><<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(p);
+    coalibi_bwd_delta_kernel<D, BF16><<<(unsigned)((rows + 8 * (256 / D) - 1) / (8 * (256 / D))), 256, 0, stream>>>(p);
   if (phases & 2)
     coalibi_bwd_a_kernel<D, BF16><<<a.B * a.Hq * p.n_qtiles, BwdALayout<D>::THREADS, BwdALayout<D>::ALLOC,
                                     stream>>>(tq, tdo, tk, tv, p);
