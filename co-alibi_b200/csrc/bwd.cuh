@@ -169,7 +169,8 @@ __device__ __forceinline__ void bwd_chunk(const uint32_t* sreg, const uint32_t* 
 // phases.  Each thread copies its S and dP columns to registers and
 // releases them at once, so the MMA warp computes S/dP of the next sub-tile
 // while this one is still in the softmax.  TMEM: S [0,128), dP [128,256),
-// dS (packed 16-bit) [256,320), dQ [320,320+D).
+// dS (packed 16-bit, two buffers so the softmax never waits for the previous
+// sub-tile's dQ) [256,384), dQ [384,384+D).
 // ---------------------------------------------------------------------------
 template <int D>
 struct BwdALayout {
@@ -186,7 +187,7 @@ struct BwdALayout {
   static constexpr int OFF_X = OFF_V + VS * TILE;  // float [2][NWG][128]: running sums handed to warpgroup w
   static constexpr int OFF_BAR = OFF_X + 2 * NWG * 128 * 4;
   static constexpr int NLINK = 4 * NWG;            // per (lane quarter, receiving warpgroup)
-  static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 7 + 2 * NLINK;
+  static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 9 + 2 * NLINK;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 16;
   static constexpr int ALLOC = BYTES + 1024;
@@ -197,7 +198,7 @@ struct BwdALayout {
   static constexpr int WARP_TMA = 4 * NWG, WARP_MMA = 4 * NWG + 1;
   static constexpr int REGS_SOFTMAX = 104, REGS_PRODUCER = 64;
   static_assert(4 * REGS_SOFTMAX + REGS_PRODUCER <= 5 * 96, "register split exceeds the launch allocation");
-  static constexpr uint32_t TM_S = 0, TM_DP = 128, TM_DS = 256, TM_DQ = 320, TM_COLS = 512;
+  static constexpr uint32_t TM_S = 0, TM_DP = 128, TM_DS = 256, TM_DQ = 384, TM_COLS = 512;
   static_assert(ALLOC <= 232448, "shared memory budget");
   static_assert(TM_DQ + D <= TM_COLS, "TMEM budget");
 };
@@ -283,9 +284,9 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
   uint64_t* s_free = s_full + 1;   // every softmax warp has S in registers
   uint64_t* dp_full = s_free + 1;
   uint64_t* dp_free = dp_full + 1;
-  uint64_t* ds_full = dp_free + 1;  // dS of the sub-tile written to TMEM
-  uint64_t* dq_done = ds_full + 1;
-  uint64_t* mma_idle = dq_done + 1;
+  uint64_t* ds_full = dp_free + 1;  // [2] dS of sub-tile n written to TMEM buffer n & 1
+  uint64_t* dq_done = ds_full + 2;  // [2] dQ(n) has read dS buffer n & 1
+  uint64_t* mma_idle = dq_done + 2;
   uint64_t* zlink = mma_idle + 1;      // [quarter][receiving warpgroup]
   uint64_t* clink = zlink + L::NLINK;  // [quarter][receiving warpgroup]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
@@ -317,8 +318,10 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
     mbar_init(s_free, 4 * L::NWG);
     mbar_init(dp_full, 1);
     mbar_init(dp_free, 4 * L::NWG);
-    mbar_init(ds_full, 4 * L::NWG);
-    mbar_init(dq_done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ds_full[i], 4 * L::NWG);
+      mbar_init(&dq_done[i], 1);
+    }
     mbar_init(mma_idle, 1);
     for (int i = 0; i < L::NLINK; ++i) {
       mbar_init(&zlink[i], 32);  // every lane of the sending warp arrives after its store
@@ -393,16 +396,17 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
       uint64_t t_idle = 0;
       while (ok && next_q < N) {
         bool progressed = false;
-        if (next_q < next_p && mbar_test(ds_full, next_q & 1)) {
+        if (next_q < next_p && mbar_test(&ds_full[next_q & 1], (next_q >> 1) & 1)) {
           tc_fence_after();
           const int ks = next_q % L::KS;
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {
             // A = dS (TMEM, 16 keys = 8 packed columns), B = K_n as (N = d, K = keys): MN-major
             const uint64_t kdesc = make_sdesc_sw128(k_addr + ks * L::TILE + kk * 16 * 128, L::KBOX, 1024);
-            umma_ts(tmem + L::TM_DQ, tmem + L::TM_DS + kk * 8, kdesc, idQ, (next_q > 0 || kk > 0) ? 1u : 0u);
+            umma_ts(tmem + L::TM_DQ, tmem + L::TM_DS + (next_q & 1) * 64 + kk * 8, kdesc, idQ,
+                    (next_q > 0 || kk > 0) ? 1u : 0u);
           }
-          umma_commit(dq_done);
+          umma_commit(&dq_done[next_q & 1]);
           umma_commit(&k_empty[ks]);
           ++next_q;
           progressed = true;
@@ -559,21 +563,21 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
         const float2 v = __ffma2_rn(m, c2, dA);                                   // dA - slope s (1 - s) c
         dso[j2] = pack2<BF16>(v.x, v.y);
       }
-      // the dS columns are free once dQ(n-1) has run
-      if (n > 0) ok = mbar_wait(dq_done, (n - 1) & 1, g);
+      // dS buffer n & 1 is free once dQ(n-2) has run
+      if (n > 1) ok = mbar_wait(&dq_done[n & 1], ((n - 2) >> 1) & 1, g);
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         tc_fence_after();
-        tmem_st16(lane_base + L::TM_DS + 16 * wg, dso);
+        tmem_st16(lane_base + L::TM_DS + (n & 1) * 64 + 16 * wg, dso);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(ds_full);
+        if (lane == 0) mbar_arrive(&ds_full[n & 1]);
       }
     }
     // epilogue: dQ = scale * (dS K); warpgroup w writes columns [w D/4, (w+1) D/4)
     if (ok && N > 0) {
-      ok = mbar_wait(dq_done, (N - 1) & 1, g);
+      ok = mbar_wait(&dq_done[(N - 1) & 1], ((N - 1) >> 1) & 1, g);
       ok = __all_sync(0xffffffffu, ok);
     }
     if (ok && N > 0) {
