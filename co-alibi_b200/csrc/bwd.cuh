@@ -617,17 +617,19 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
-// 3. pass B: dK, dV
+// 3a. pass B for D = 64: dK, dV
+//
+// One CTA per 128 keys of a kv head, one softmax warpgroup (a thread per query
+// row, the block's 128 keys as four 32-key chunks restarted from pass A's
+// carries), accumulators dV = P^T dO and dK = dS^T Q with M = 128 keys.  (D = 128
+// uses coalibi_bwd_b128_kernel below.)
 // ---------------------------------------------------------------------------
 template <int D>
 struct BwdBLayout {
-  static constexpr bool TRANS = (D == 128);      // accumulate dV^T / dK^T (M = D)
-  static constexpr int KB = TRANS ? 64 : 128;    // keys per CTA
-  static constexpr int NS = TRANS ? 2 : 1;       // S / dS TMEM buffers
-  // D = 128: two softmax warpgroups work on every iteration together, warpgroup w
-  // on keys [32w, 32w+32) of the block (pass A's carries every 32 keys make the
-  // halves independent).  D = 64: one warpgroup, all 128 keys.
-  static constexpr int NWG = NS;
+  static_assert(D == 64, "pass B for D = 128 is coalibi_bwd_b128_kernel");
+  static constexpr int KB = 128;                 // keys per CTA
+  static constexpr int NS = 1;                   // S / dS TMEM buffers
+  static constexpr int NWG = 1;
   static constexpr int THREADS = 128 * NWG + 64; // + TMA warp + MMA warp
   static constexpr int WARP_TMA = 4 * NWG, WARP_MMA = 4 * NWG + 1;
   static constexpr int QS = 2, PS = 2;           // Q/dO and P/dP shared-memory stages
@@ -645,12 +647,12 @@ struct BwdBLayout {
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 16;
   static constexpr int ALLOC = BYTES + 1024;
-  static constexpr uint32_t TM_S = 0;                 // NS buffers of KB columns
-  static constexpr uint32_t TM_DS = NS * KB;          // NS buffers of KB columns
-  static constexpr uint32_t TM_DV = 2 * NS * KB;      // TRANS: KB columns (lanes = d); else D columns (lanes = keys)
-  static constexpr uint32_t TM_DK = TM_DV + (TRANS ? KB : D);
+  static constexpr uint32_t TM_S = 0;                 // KB columns
+  static constexpr uint32_t TM_DS = KB;               // KB columns
+  static constexpr uint32_t TM_DV = 2 * KB;           // D columns (lanes = keys)
+  static constexpr uint32_t TM_DK = TM_DV + D;
   static constexpr uint32_t TM_COLS = 512;
-  static_assert(TM_DK + (TRANS ? KB : D) <= 512, "TMEM budget");
+  static_assert(TM_DK + D <= 512, "TMEM budget");
 };
 
 __device__ __forceinline__ void decode_block(int L, int n_heads, int n_blocks, int& hk, int& blk) {
@@ -767,10 +769,8 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
   } else if (warp == L::WARP_MMA) {
     if (lane == 0 && NIT > 0) {
       constexpr uint32_t idS = make_idesc_f16(BF16, 128, KB, false, false);
-      // TRANS: dV^T[d][key] = dO^T[d][row] P[row][key]  (A = dO^T MN-major, B = P MN-major), M = D, N = KB
-      // else : dV[key][d]   = P^T[key][row] dO[row][d]  (A = P^T MN-major, B = dO MN-major),  M = KB, N = D
-      constexpr uint32_t idAcc = L::TRANS ? make_idesc_f16(BF16, D, KB, true, true)
-                                          : make_idesc_f16(BF16, KB, D, true, true);
+      // dV[key][d] = P^T[key][row] dO[row][d]  (A = P^T MN-major, B = dO MN-major), M = KB, N = D
+      constexpr uint32_t idAcc = make_idesc_f16(BF16, KB, D, true, true);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
       const uint32_t qdo_addr = smem_u32(sQDO), p_addr = smem_u32(sP);
       auto issue_SdS = [&](int it) {
@@ -815,19 +815,11 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
 #pragma unroll
           for (int kk = 0; kk < 128 / 16; ++kk) {  // K = 128 query rows, 16 per MMA
             const uint32_t ko = kk * 16 * 128;        // 16 rows of 128 bytes
-            if (L::TRANS) {
-              // A: dO^T / Q^T (MN = d, 64-wide blocks one box apart), B: P / dP (MN = keys, one block)
-              umma_ss(tmem + L::TM_DV, make_sdesc_sw128(da + ko, L::QBOX, 1024),
-                      make_sdesc_sw128(pa + ko, L::PB, 1024), idAcc, (acc || kk > 0) ? 1u : 0u);
-              umma_ss(tmem + L::TM_DK, make_sdesc_sw128(qa + ko, L::QBOX, 1024),
-                      make_sdesc_sw128(dpa + ko, L::PB, 1024), idAcc, (acc || kk > 0) ? 1u : 0u);
-            } else {
-              // A: P^T / dP^T (MN = keys, two 64-key blocks 128*128 bytes apart), B: dO / Q (MN = d)
-              umma_ss(tmem + L::TM_DV, make_sdesc_sw128(pa + ko, 128 * 128, 1024),
-                      make_sdesc_sw128(da + ko, L::QBOX, 1024), idAcc, (acc || kk > 0) ? 1u : 0u);
-              umma_ss(tmem + L::TM_DK, make_sdesc_sw128(dpa + ko, 128 * 128, 1024),
-                      make_sdesc_sw128(qa + ko, L::QBOX, 1024), idAcc, (acc || kk > 0) ? 1u : 0u);
-            }
+            // A: P^T / dP^T (MN = keys, two 64-key blocks 128*128 bytes apart), B: dO / Q (MN = d)
+            umma_ss(tmem + L::TM_DV, make_sdesc_sw128(pa + ko, 128 * 128, 1024),
+                    make_sdesc_sw128(da + ko, L::QBOX, 1024), idAcc, (acc || kk > 0) ? 1u : 0u);
+            umma_ss(tmem + L::TM_DK, make_sdesc_sw128(dpa + ko, 128 * 128, 1024),
+                    make_sdesc_sw128(qa + ko, L::QBOX, 1024), idAcc, (acc || kk > 0) ? 1u : 0u);
           }
           umma_commit(&pp_empty[ps]);
           umma_commit(&qdo_empty[st]);
@@ -835,15 +827,10 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
           progressed = true;
         }
         if (next_s < NIT) {
-          // TMEM buffer of S/dS(next_s): with two buffers, free once P/dP(next_s - 2) was
-          // published (the softmax read S/dS before that); with one, once s_free says so.
-          bool buf_free;
-          if (L::NS == 2) {
-            buf_free = next_s < next_d + 2;
-          } else {
-            if (sfree_seen < next_s && mbar_test(s_free, sfree_seen & 1)) ++sfree_seen;
-            buf_free = sfree_seen >= next_s;
-          }
+          // the single TMEM buffer of S/dS(next_s) is free once s_free says the
+          // softmax read S/dS(next_s - 1)
+          if (sfree_seen < next_s && mbar_test(s_free, sfree_seen & 1)) ++sfree_seen;
+          const bool buf_free = sfree_seen >= next_s;
           if (buf_free && mbar_test(&qdo_full[next_s % L::QS], (next_s / L::QS) & 1)) {
             issue_SdS(next_s);
             ++next_s;
@@ -965,92 +952,53 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
       tc_fence_before();
       mbar_arrive(&pp_full[ps]);
     }
-    // epilogue: every warpgroup covers all 128 TMEM lanes; with two warpgroups
-    // (transposed accumulators, lanes = d) each writes its half of the key columns
+    // epilogue: lane t = key, columns = d
     const int bkv = hk;
-    if (!L::TRANS && wg != 0) {
-    } else if (NIT > 0) {
+    if (NIT > 0) {
       if (ok) {
         ok = mbar_wait(acc_done, 0, g);
         ok = __all_sync(0xffffffffu, ok);
       }
       if (ok) {
         tc_fence_after();
-        if (L::TRANS) {
-          // lane t = d; columns = keys of this block
-          const int d = t_row;
+        const int key = key0 + t_row;
+        uint8_t* dvrow = static_cast<uint8_t*>(p.dv) + ((size_t)bkv * p.Skv + key) * D * 2;
+        uint8_t* dkrow = static_cast<uint8_t*>(p.dk) + ((size_t)bkv * p.Skv + key) * D * 2;
 #pragma unroll 1
-          for (int c = wkey0 / 32; c < (wkey0 + WKB) / 32; ++c) {
-            uint32_t rv[32], rk[32];
-            tmem_ld32(lane_base + L::TM_DV + c * 32, rv);
-            tmem_ld32(lane_base + L::TM_DK + c * 32, rk);
-            tmem_ld_wait32(rv);
-            tmem_ld_fence32(rk);
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t rv[32], rk[32];
+          tmem_ld32(lane_base + L::TM_DV + c * 32, rv);
+          tmem_ld32(lane_base + L::TM_DK + c * 32, rk);
+          tmem_ld_wait32(rv);
+          tmem_ld_fence32(rk);
+          if (key < p.Skv) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int key = key0 + c * 32 + j;
-              if (key < p.Skv) {
-                const size_t o = ((size_t)bkv * p.Skv + key) * D + d;
-                const uint32_t pv = pack2<BF16>(__uint_as_float(rv[j]), 0.f);
-                const uint32_t pk = pack2<BF16>(__uint_as_float(rk[j]) * p.sm_scale, 0.f);
-                static_cast<uint16_t*>(p.dv)[o] = (uint16_t)(pv & 0xffffu);
-                static_cast<uint16_t*>(p.dk)[o] = (uint16_t)(pk & 0xffffu);
-              }
-            }
-          }
-        } else {
-          // lane t = key; columns = d
-          const int key = key0 + t_row;
-          uint8_t* dvrow = static_cast<uint8_t*>(p.dv) + ((size_t)bkv * p.Skv + key) * D * 2;
-          uint8_t* dkrow = static_cast<uint8_t*>(p.dk) + ((size_t)bkv * p.Skv + key) * D * 2;
-#pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t rv[32], rk[32];
-            tmem_ld32(lane_base + L::TM_DV + c * 32, rv);
-            tmem_ld32(lane_base + L::TM_DK + c * 32, rk);
-            tmem_ld_wait32(rv);
-            tmem_ld_fence32(rk);
-            if (key < p.Skv) {
-#pragma unroll
-              for (int v4 = 0; v4 < 4; ++v4) {
-                uint4 a, bb;
-                a.x = pack2<BF16>(__uint_as_float(rv[8 * v4 + 0]), __uint_as_float(rv[8 * v4 + 1]));
-                a.y = pack2<BF16>(__uint_as_float(rv[8 * v4 + 2]), __uint_as_float(rv[8 * v4 + 3]));
-                a.z = pack2<BF16>(__uint_as_float(rv[8 * v4 + 4]), __uint_as_float(rv[8 * v4 + 5]));
-                a.w = pack2<BF16>(__uint_as_float(rv[8 * v4 + 6]), __uint_as_float(rv[8 * v4 + 7]));
-                const float s = p.sm_scale;
-                bb.x = pack2<BF16>(__uint_as_float(rk[8 * v4 + 0]) * s, __uint_as_float(rk[8 * v4 + 1]) * s);
-                bb.y = pack2<BF16>(__uint_as_float(rk[8 * v4 + 2]) * s, __uint_as_float(rk[8 * v4 + 3]) * s);
-                bb.z = pack2<BF16>(__uint_as_float(rk[8 * v4 + 4]) * s, __uint_as_float(rk[8 * v4 + 5]) * s);
-                bb.w = pack2<BF16>(__uint_as_float(rk[8 * v4 + 6]) * s, __uint_as_float(rk[8 * v4 + 7]) * s);
-                reinterpret_cast<uint4*>(dvrow + c * 64)[v4] = a;
-                reinterpret_cast<uint4*>(dkrow + c * 64)[v4] = bb;
-              }
+            for (int v4 = 0; v4 < 4; ++v4) {
+              uint4 a, bb;
+              a.x = pack2<BF16>(__uint_as_float(rv[8 * v4 + 0]), __uint_as_float(rv[8 * v4 + 1]));
+              a.y = pack2<BF16>(__uint_as_float(rv[8 * v4 + 2]), __uint_as_float(rv[8 * v4 + 3]));
+              a.z = pack2<BF16>(__uint_as_float(rv[8 * v4 + 4]), __uint_as_float(rv[8 * v4 + 5]));
+              a.w = pack2<BF16>(__uint_as_float(rv[8 * v4 + 6]), __uint_as_float(rv[8 * v4 + 7]));
+              const float s = p.sm_scale;
+              bb.x = pack2<BF16>(__uint_as_float(rk[8 * v4 + 0]) * s, __uint_as_float(rk[8 * v4 + 1]) * s);
+              bb.y = pack2<BF16>(__uint_as_float(rk[8 * v4 + 2]) * s, __uint_as_float(rk[8 * v4 + 3]) * s);
+              bb.z = pack2<BF16>(__uint_as_float(rk[8 * v4 + 4]) * s, __uint_as_float(rk[8 * v4 + 5]) * s);
+              bb.w = pack2<BF16>(__uint_as_float(rk[8 * v4 + 6]) * s, __uint_as_float(rk[8 * v4 + 7]) * s);
+              reinterpret_cast<uint4*>(dvrow + c * 64)[v4] = a;
+              reinterpret_cast<uint4*>(dkrow + c * 64)[v4] = bb;
             }
           }
         }
       }
     } else {
       // no query row sees these keys: their gradients are zero
-      if (L::TRANS) {
-        const int d = t_row;
-        for (int j = wkey0; j < wkey0 + WKB; ++j) {
-          const int key = key0 + j;
-          if (key < p.Skv) {
-            const size_t o = ((size_t)bkv * p.Skv + key) * D + d;
-            static_cast<uint16_t*>(p.dv)[o] = 0;
-            static_cast<uint16_t*>(p.dk)[o] = 0;
-          }
-        }
-      } else if (wg == 0) {
-        const int key = key0 + t_row;
-        if (key < p.Skv) {
-          uint4* dvrow = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.dv) + ((size_t)bkv * p.Skv + key) * D * 2);
-          uint4* dkrow = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.dk) + ((size_t)bkv * p.Skv + key) * D * 2);
-          for (int v4 = 0; v4 < D / 8; ++v4) {
-            dvrow[v4] = make_uint4(0, 0, 0, 0);
-            dkrow[v4] = make_uint4(0, 0, 0, 0);
-          }
+      const int key = key0 + t_row;
+      if (key < p.Skv) {
+        uint4* dvrow = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.dv) + ((size_t)bkv * p.Skv + key) * D * 2);
+        uint4* dkrow = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.dk) + ((size_t)bkv * p.Skv + key) * D * 2);
+        for (int v4 = 0; v4 < D / 8; ++v4) {
+          dvrow[v4] = make_uint4(0, 0, 0, 0);
+          dkrow[v4] = make_uint4(0, 0, 0, 0);
         }
       }
     }
@@ -1483,7 +1431,9 @@ inline int bwd_launch_t(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigne
   p.n_qtiles = (a.Sq + 127) / 128;
   p.n_kvtiles = (a.Skv + 127) / 128;
   p.n_kb32 = (a.Skv + 31) / 32;
-  const int kb_b = (D == 128) ? BwdB128Layout::KB : BwdBLayout<D>::KB;
+  int kb_b;  // keys per pass-B CTA
+  if constexpr (D == 128) kb_b = BwdB128Layout::KB;
+  else kb_b = BwdBLayout<D>::KB;
   p.n_blocks = (a.Skv + kb_b - 1) / kb_b;
   p.sq_pad = p.n_qtiles * 128;
 
