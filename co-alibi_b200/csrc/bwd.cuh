@@ -1017,28 +1017,33 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
 // 3b. pass B for D = 128: 128-key blocks, four softmax warpgroups
 //
 // One CTA per 128 keys of a kv head, so S = Q K^T and dP = dO V^T run at
-// N = 128 and every query tile loaded from L2 serves twice the keys of a
-// 64-key block.  Warpgroup w takes keys [32w, 32w+32) of every query tile; pass
-// A's carries every 32 keys make the four chunks independent (no exchange).
-// Each thread copies its S and dP columns to registers and releases them, so
-// S/dP of the next tile run while this one is in the softmax.  P and dS share
-// one 32 KB shared-memory buffer in turn: P feeds dV^T += dO^T P, then dS
-// feeds dK^T += Q^T dS (both M = D = 128, N = 128 keys).  TMEM: S [0,128),
-// dP [128,256), dV^T [256,384), dK^T [384,512) (lanes = d, columns = keys).
+// N = 128 and every query tile loaded from L2 serves 128 keys.  Warpgroup w
+// takes keys [32w, 32w+32) of every query tile; pass A's carries every 32 keys
+// make the four chunks independent (no exchange).  The per-key maths run in two
+// phases so that P reaches its MMA before dP is even needed: phase A (S only)
+// forms the sigmoids and P and writes P; dV^T += dO^T P then runs and frees dO
+// for the next tile's load while phase B (needs dP) forms dS, which goes to its
+// own buffer for dK^T += Q^T dS.  Shared memory: K, V (64 KB), a two-deep Q ring
+// (64 KB), one dO tile (32 KB), P and dS tiles (32 KB each) = 224 KB.  Each
+// thread copies its S and dP columns to registers and releases them, so S/dP of
+// the next tile run during this one's softmax.  TMEM: S [0,128), dP [128,256),
+// dV^T [256,384), dK^T [384,512) (lanes = d, columns = keys).
 // ---------------------------------------------------------------------------
 struct BwdB128Layout {
   static constexpr int D = 128, KB = 128, NWG = 4;
-  static constexpr int QS = 2;                    // Q/dO stages
+  static constexpr int QS = 2;                    // Q stages (dO has one)
   static constexpr int BOX = 128 * 128;           // one [128 rows][64 cols] TMA box
   static constexpr int KTILE = KB * D * 2;        // 32 KB
   static constexpr int QB = 128 * D * 2;          // 32 KB
   static constexpr int PBLK = 128 * 64 * 2;       // [128 query rows][64 keys], 16 KB
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = KTILE;
-  static constexpr int OFF_QDO = 2 * KTILE;       // QS stages of (Q, dO)
-  static constexpr int OFF_PB = OFF_QDO + QS * 2 * QB;  // P, then dS, of one query tile
-  static constexpr int OFF_BAR = OFF_PB + 2 * PBLK;
-  static constexpr int NBAR = 1 + 2 * QS + 6;
+  static constexpr int OFF_Q = 2 * KTILE;         // QS stages
+  static constexpr int OFF_DO = OFF_Q + QS * QB;
+  static constexpr int OFF_P = OFF_DO + QB;       // P of one query tile (two 64-key blocks)
+  static constexpr int OFF_DS = OFF_P + 2 * PBLK; // dS of one query tile
+  static constexpr int OFF_BAR = OFF_DS + 2 * PBLK;
+  static constexpr int NBAR = 1 + 2 * QS + 2 + 12;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 16;
   static constexpr int ALLOC = BYTES + 1024;
@@ -1049,6 +1054,60 @@ struct BwdB128Layout {
   static constexpr uint32_t TM_S = 0, TM_DP = 128, TM_DV = 256, TM_DK = 384, TM_COLS = 512;
   static_assert(ALLOC <= 232448, "shared memory budget");
 };
+
+// Phase A of a 32-key chunk (S only): sigmoids kept in sg, P kept in sreg (over
+// the scores) and packed into po; zs is the sigmoid suffix from the chunk's first
+// key on (inclusive) and is advanced past the chunk.
+template <bool MASK, bool BF16>
+__device__ __forceinline__ void bwd_b_phase_a(uint32_t* sreg, float* sg, uint32_t* po, int key0, int lim,
+                                              float c_t, float c_a, float slope2, float lse2, float& zs) {
+#pragma unroll
+  for (int j2 = 0; j2 < 16; ++j2) {
+    const int j = 2 * j2;
+    const float2 x = make_float2(__uint_as_float(sreg[j]), __uint_as_float(sreg[j + 1]));
+    const float2 u = __fmul2_rn(x, make_float2(c_t, c_t));
+    float2 s = __ffma2_rn(make_float2(0.5f, 0.5f), make_float2(tanh_approx(u.x), tanh_approx(u.y)),
+                          make_float2(0.5f, 0.5f));
+    if (MASK && key0 + j >= lim) s.x = 0.f;
+    if (MASK && key0 + j + 1 >= lim) s.y = 0.f;
+    float2 z;  // sigmoid suffix from each key on (inclusive)
+    z.x = zs;
+    z.y = zs - s.x;
+    zs = z.y - s.y;
+    const float2 e = __ffma2_rn(make_float2(-slope2, -slope2), z,
+                                __ffma2_rn(x, make_float2(c_a, c_a), make_float2(-lse2, -lse2)));
+    float2 P = make_float2(ex2_approx(e.x), ex2_approx(e.y));
+    if (MASK && key0 + j >= lim) P.x = 0.f;
+    if (MASK && key0 + j + 1 >= lim) P.y = 0.f;
+    sg[j] = s.x;
+    sg[j + 1] = s.y;
+    sreg[j] = __float_as_uint(P.x);
+    sreg[j + 1] = __float_as_uint(P.y);
+    po[j2] = pack2<BF16>(P.x, P.y);
+  }
+}
+
+// Phase B on 16 keys (needs dP): dA = P (dP - delta), c = running dA prefix,
+// dS = dA - slope s (1 - s) c, packed into dso.
+template <bool BF16>
+__device__ __forceinline__ void bwd_b_phase_b(const uint32_t* preg, const float* sg, const uint32_t* dpr,
+                                              float slope, float delta, float& cacc, uint32_t* dso) {
+#pragma unroll
+  for (int j2 = 0; j2 < 8; ++j2) {
+    const int j = 2 * j2;
+    const float2 P = make_float2(__uint_as_float(preg[j]), __uint_as_float(preg[j + 1]));
+    const float2 dA = __fmul2_rn(
+        P, __fadd2_rn(make_float2(__uint_as_float(dpr[j]), __uint_as_float(dpr[j + 1])), make_float2(-delta, -delta)));
+    float2 c;  // dA prefix up to each key (inclusive)
+    c.x = cacc + dA.x;
+    c.y = c.x + dA.y;
+    cacc = c.y;
+    const float2 s2 = make_float2(sg[j], sg[j + 1]);
+    const float2 sp = __ffma2_rn(make_float2(-s2.x, -s2.y), s2, s2);  // s (1 - s)
+    const float2 dp = __ffma2_rn(__fmul2_rn(sp, make_float2(-slope, -slope)), c, dA);
+    dso[j2] = pack2<BF16>(dp.x, dp.y);
+  }
+}
 
 template <bool BF16>
 __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
@@ -1061,17 +1120,25 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem + L::OFF_K;
   uint8_t* sV = smem + L::OFF_V;
-  uint8_t* sQDO = smem + L::OFF_QDO;
-  uint8_t* sPB = smem + L::OFF_PB;
+  uint8_t* sQ = smem + L::OFF_Q;
+  uint8_t* sDO = smem + L::OFF_DO;
+  uint8_t* sP = smem + L::OFF_P;
+  uint8_t* sDS = smem + L::OFF_DS;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* kv_full = bars;
-  uint64_t* qdo_full = kv_full + 1;
-  uint64_t* qdo_empty = qdo_full + L::QS;
-  uint64_t* s_full = qdo_empty + L::QS;  // S and dP of the tile are in TMEM
-  uint64_t* s_free = s_full + 1;         // every softmax warp copied them out
-  uint64_t* buf_full = s_free + 1;       // use k of the P/dS buffer written (k = 2 it: P, 2 it + 1: dS)
-  uint64_t* buf_empty = buf_full + 1;    // use k consumed by its MMA
-  uint64_t* acc_done = buf_empty + 1;
+  uint64_t* q_full = kv_full + 1;       // [QS]
+  uint64_t* q_empty = q_full + L::QS;   // [QS] dK^T of the tile read Q
+  uint64_t* do_full = q_empty + L::QS;
+  uint64_t* do_empty = do_full + 1;     // dV^T of the tile read dO
+  uint64_t* s_full = do_empty + 1;      // S of the tile in TMEM
+  uint64_t* s_free = s_full + 1;        // every softmax warp copied S out
+  uint64_t* dp_full = s_free + 1;
+  uint64_t* dp_free = dp_full + 1;
+  uint64_t* p_full = dp_free + 1;       // P of the tile written
+  uint64_t* p_empty = p_full + 1;       // dV^T read it
+  uint64_t* ds_full = p_empty + 1;
+  uint64_t* ds_empty = ds_full + 1;     // dK^T read it
+  uint64_t* acc_done = ds_empty + 1;
   uint64_t* mma_idle = acc_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
@@ -1092,13 +1159,19 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
     for (int i = 0; i < L::QS; ++i) {
-      mbar_init(&qdo_full[i], 1);
-      mbar_init(&qdo_empty[i], 1);
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
     }
+    mbar_init(do_full, 1);
+    mbar_init(do_empty, 1);
     mbar_init(s_full, 1);
     mbar_init(s_free, 4 * L::NWG);
-    mbar_init(buf_full, 4 * L::NWG);
-    mbar_init(buf_empty, 1);
+    mbar_init(dp_full, 1);
+    mbar_init(dp_free, 4 * L::NWG);
+    mbar_init(p_full, 4 * L::NWG);
+    mbar_init(p_empty, 1);
+    mbar_init(ds_full, 4 * L::NWG);
+    mbar_init(ds_empty, 1);
     mbar_init(acc_done, 1);
     mbar_init(mma_idle, 1);
     *abort_flag = 0;
@@ -1127,27 +1200,37 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
         tma_load_3d(sK + bx * L::BOX, &tmK, kv_full, bx * 64, key0, hk);
         tma_load_3d(sV + bx * L::BOX, &tmV, kv_full, bx * 64, key0, hk);
       }
-      int nq = 0;
-      for (int it = 0; it < NIT; ++it) {
-        const int hh = gkv * G + it / nM;
-        const int m = m_start + it % nM;
-        const int bhq = b * p.Hq + hh;
+      int nq = 0, ndo = 0;
+      bool ok = true;
+      auto bhq_of = [&](int it) { return b * p.Hq + gkv * G + it / nM; };
+      auto m_of = [&](int it) { return m_start + it % nM; };
+      auto load_q = [&](int it) -> bool {
         const int st = it % L::QS;
-        if (!mbar_wait(&qdo_empty[st], ((it / L::QS) & 1) ^ 1, g)) break;
-        mbar_arrive_expect_tx(&qdo_full[st], 2 * L::QB);
-        uint8_t* sq = sQDO + st * 2 * L::QB;
+        if (!mbar_wait(&q_empty[st], ((it / L::QS) & 1) ^ 1, g)) return false;
+        mbar_arrive_expect_tx(&q_full[st], L::QB);
 #pragma unroll
-        for (int bx = 0; bx < D / 64; ++bx) {
-          tma_load_3d(sq + bx * L::BOX, &tmQ, &qdo_full[st], bx * 64, m * 128, bhq);
-          tma_load_3d(sq + L::QB + bx * L::BOX, &tmDO, &qdo_full[st], bx * 64, m * 128, bhq);
-        }
+        for (int bx = 0; bx < D / 64; ++bx)
+          tma_load_3d(sQ + st * L::QB + bx * L::BOX, &tmQ, &q_full[st], bx * 64, m_of(it) * 128, bhq_of(it));
         ++nq;
+        return true;
+      };
+      // Q runs a tile ahead of dO: dO(it) waits for dV^T(it - 1), Q(it + 1) for dK^T(it - 1)
+      ok = load_q(0);
+      for (int it = 0; ok && it < NIT; ++it) {
+        if (!(ok = mbar_wait(do_empty, (it & 1) ^ 1, g))) break;
+        mbar_arrive_expect_tx(do_full, L::QB);
+#pragma unroll
+        for (int bx = 0; bx < D / 64; ++bx)
+          tma_load_3d(sDO + bx * L::BOX, &tmDO, do_full, bx * 64, m_of(it) * 128, bhq_of(it));
+        ++ndo;
+        if (it + 1 < NIT) ok = load_q(it + 1);
       }
       mbar_drain(kv_full, 0, g.timeout_ns);
       for (int s = 0; s < L::QS; ++s) {
         const int uses = (nq > s) ? (nq - 1 - s) / L::QS + 1 : 0;
-        if (uses > 0) mbar_drain(&qdo_full[s], (uses - 1) & 1, g.timeout_ns);
+        if (uses > 0) mbar_drain(&q_full[s], (uses - 1) & 1, g.timeout_ns);
       }
+      if (ndo > 0) mbar_drain(do_full, (ndo - 1) & 1, g.timeout_ns);
     }
   } else if (warp == L::WARP_MMA) {
     if (lane == 0 && NIT > 0) {
@@ -1155,59 +1238,71 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
       // dV^T[d][key] = dO^T[d][row] P[row][key], dK^T = Q^T dS: A MN-major (d), B MN-major (keys)
       constexpr uint32_t idAcc = make_idesc_f16(BF16, D, KB, true, true);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-      const uint32_t qdo_addr = smem_u32(sQDO), pb_addr = smem_u32(sPB);
+      const uint32_t q_addr = smem_u32(sQ), do_addr = smem_u32(sDO);
+      const uint32_t p_addr = smem_u32(sP), ds_addr = smem_u32(sDS);
       bool ok = mbar_wait(kv_full, 0, g);
-      int next_sd = 0, next_u = 0;
+      if (ok) tc_fence_after();
+      int next_s = 0, next_p = 0, next_v = 0, next_k = 0;
       int idle = 0;
       uint64_t t_idle = 0;
-      // consumer of the P/dS buffer (dV^T for P, dK^T for dS): it frees the buffer
-      // for the softmax and, after dK^T, the Q/dO stage
-      auto try_consume = [&]() -> bool {
-        if (!(next_u < 2 * next_sd && mbar_test(buf_full, next_u & 1))) return false;
-        tc_fence_after();
-        const int it = next_u >> 1;
-        const int st = it % L::QS;
-        const uint32_t qa = qdo_addr + st * 2 * L::QB;
-        const uint32_t aa = (next_u & 1) ? qa : qa + L::QB;      // Q^T for dK, dO^T for dV
-        const uint32_t acc_t = tmem + ((next_u & 1) ? L::TM_DK : L::TM_DV);
+      auto acc_mma = [&](uint32_t acc_t, uint32_t a_base, uint32_t b_base, bool first) {
 #pragma unroll
         for (int kk = 0; kk < 128 / 16; ++kk) {  // K = 128 query rows, 16 per MMA
           const uint32_t ko = kk * 16 * 128;
-          umma_ss(acc_t, make_sdesc_sw128(aa + ko, L::BOX, 1024), make_sdesc_sw128(pb_addr + ko, L::PBLK, 1024),
-                  idAcc, (it > 0 || kk > 0) ? 1u : 0u);
+          umma_ss(acc_t, make_sdesc_sw128(a_base + ko, L::BOX, 1024), make_sdesc_sw128(b_base + ko, L::PBLK, 1024),
+                  idAcc, (!first || kk > 0) ? 1u : 0u);
         }
-        umma_commit(buf_empty);
-        if (next_u & 1) umma_commit(&qdo_empty[st]);
-        ++next_u;
-        return true;
       };
-      while (ok && next_u < 2 * NIT) {
-        if (try_consume()) {
+      while (ok && next_k < NIT) {
+        // dV^T(it): frees dO(it) for the next tile's load -- first
+        if (next_v < next_p && mbar_test(p_full, next_v & 1)) {
+          tc_fence_after();
+          acc_mma(tmem + L::TM_DV, do_addr, p_addr, next_v == 0);
+          umma_commit(p_empty);
+          umma_commit(do_empty);
+          ++next_v;
           idle = 0;
           t_idle = 0;
           continue;
         }
-        if (next_sd < NIT && (next_sd == 0 || mbar_test(s_free, (next_sd - 1) & 1)) &&
-            mbar_test(&qdo_full[next_sd % L::QS], (next_sd / L::QS) & 1)) {
+        if (next_k < next_v && mbar_test(ds_full, next_k & 1)) {
           tc_fence_after();
-          const uint32_t qa = qdo_addr + (next_sd % L::QS) * 2 * L::QB, da = qa + L::QB;
+          acc_mma(tmem + L::TM_DK, q_addr + (next_k % L::QS) * L::QB, ds_addr, next_k == 0);
+          umma_commit(ds_empty);
+          umma_commit(&q_empty[next_k % L::QS]);
+          if (next_k + 1 == NIT) umma_commit(acc_done);
+          ++next_k;
+          idle = 0;
+          t_idle = 0;
+          continue;
+        }
+        if (next_p < next_s && (next_p == 0 || mbar_test(dp_free, (next_p - 1) & 1)) &&
+            mbar_test(do_full, next_p & 1)) {
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t o = (kk >> 2) * L::BOX + (kk & 3) * 32;
+            umma_ss(tmem + L::TM_DP, make_sdesc_sw128(do_addr + o, 16, 1024), make_sdesc_sw128(v_addr + o, 16, 1024),
+                    idS, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(dp_full);
+          ++next_p;
+          idle = 0;
+          t_idle = 0;
+          continue;
+        }
+        if (next_s < NIT && (next_s == 0 || mbar_test(s_free, (next_s - 1) & 1)) &&
+            mbar_test(&q_full[next_s % L::QS], (next_s / L::QS) & 1)) {
+          tc_fence_after();
+          const uint32_t qa = q_addr + (next_s % L::QS) * L::QB;
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t o = (kk >> 2) * L::BOX + (kk & 3) * 32;
             umma_ss(tmem + L::TM_S, make_sdesc_sw128(qa + o, 16, 1024), make_sdesc_sw128(k_addr + o, 16, 1024), idS,
                     kk > 0 ? 1u : 0u);
           }
-          // the MMA thread blocks while the pipe drains what it issued: give a
-          // waiting buffer consumer its turn between the two halves
-          try_consume();
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t o = (kk >> 2) * L::BOX + (kk & 3) * 32;
-            umma_ss(tmem + L::TM_DP, make_sdesc_sw128(da + o, 16, 1024), make_sdesc_sw128(v_addr + o, 16, 1024), idS,
-                    kk > 0 ? 1u : 0u);
-          }
           umma_commit(s_full);
-          ++next_sd;
+          ++next_s;
           idle = 0;
           t_idle = 0;
           continue;
@@ -1223,7 +1318,6 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
           }
         }
       }
-      if (ok) umma_commit(acc_done);
       umma_commit(mma_idle);
       mbar_drain(mma_idle, 0, g.timeout_ns);
     }
@@ -1263,7 +1357,7 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
     RowIn nxt = load_row(0, gkv * G, m_start);
     int hh = gkv * G, m = m_start;          // head and query tile of iteration it
     int hh_n = hh + (nM == 1 ? 1 : 0), m_n = (nM == 1) ? m_start : m_start + 1;  // of it + 1
-    // this thread's row in the 128B-swizzled P/dS tile: keys of block (wg >> 1), 16-byte chunks (wg & 1) * 4 + u
+    // this thread's row in the 128B-swizzled P/dS tiles: keys of block (wg >> 1), 16-byte chunks (wg & 1) * 4 + u
     const uint32_t rsw = t_row & 7;
     const uint32_t pb_row = (uint32_t)(wg >> 1) * L::PBLK + (t_row >> 3) * 1024 + rsw * 128;
     for (int it = 0; it < NIT; ++it) {
@@ -1280,50 +1374,67 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
       const int lim = row_ok ? (p.causal ? min(row + 1, p.Skv) : p.Skv) : 0;
       const bool masked =
           (m * 128 + 128 > p.Sq) || (ckey0 + 32 > p.Skv) || (p.causal && ckey0 + 31 > m * 128);
+      // ---- phase A: S -> sigmoids and P
       ok = mbar_wait(s_full, it & 1, g);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      uint32_t sreg[32], dsreg[32];
+      uint32_t sreg[32];
+      float sg[32];
       tmem_ld32(lane_base + L::TM_S + 32 * wg, sreg);
-      tmem_ld32(lane_base + L::TM_DP + 32 * wg, dsreg);
       tmem_ld_wait32(sreg);
-      tmem_ld_fence32(dsreg);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_free);
-      uint32_t po[16], dpo[16];
-      if (masked)
-        bwd_chunk<true, BF16, true>(sreg, dsreg, ckey0, lim, c_t, c_a, slope, slope2, cur.lse2 * kLog2e,
-                                    cur.delta, zs, cacc, dpo, po);
-      else
-        bwd_chunk<false, BF16, true>(sreg, dsreg, ckey0, lim, c_t, c_a, slope, slope2, cur.lse2 * kLog2e,
-                                     cur.delta, zs, cacc, dpo, po);
-      // use 2 it of the buffer (P) once use 2 it - 1 (dS of the previous tile) was consumed
-      if (it > 0) ok = mbar_wait(buf_empty, 1, g);
+      {
+        uint32_t po[16];
+        if (masked)
+          bwd_b_phase_a<true, BF16>(sreg, sg, po, ckey0, lim, c_t, c_a, slope2, cur.lse2 * kLog2e, zs);
+        else
+          bwd_b_phase_a<false, BF16>(sreg, sg, po, ckey0, lim, c_t, c_a, slope2, cur.lse2 * kLog2e, zs);
+        // P of this tile once dV^T of the previous one read the P tile
+        if (it > 0) ok = mbar_wait(p_empty, (it - 1) & 1, g);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t off = pb_row + ((((uint32_t)(wg & 1) * 4 + u) ^ rsw) << 4);
+          *reinterpret_cast<uint4*>(sP + off) = make_uint4(po[4 * u], po[4 * u + 1], po[4 * u + 2], po[4 * u + 3]);
+        }
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      // ---- phase B: dP -> dS
+      ok = mbar_wait(dp_full, it & 1, g);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t dso[16];
+#pragma unroll
+      for (int hh2 = 0; hh2 < 2; ++hh2) {
+        uint32_t dpr[16];
+        tmem_ld16(lane_base + L::TM_DP + 32 * wg + 16 * hh2, dpr);
+        tmem_ld_wait16(dpr);
+        if (hh2 == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(dp_free);
+        }
+        bwd_b_phase_b<BF16>(sreg + 16 * hh2, sg + 16 * hh2, dpr, slope, cur.delta, cacc, dso + 8 * hh2);
+      }
+      // dS of this tile once dK^T of the previous one read the dS tile
+      if (it > 0) ok = mbar_wait(ds_empty, (it - 1) & 1, g);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const uint32_t off = pb_row + ((((uint32_t)(wg & 1) * 4 + u) ^ rsw) << 4);
-        *reinterpret_cast<uint4*>(sPB + off) = make_uint4(po[4 * u], po[4 * u + 1], po[4 * u + 2], po[4 * u + 3]);
+        *reinterpret_cast<uint4*>(sDS + off) = make_uint4(dso[4 * u], dso[4 * u + 1], dso[4 * u + 2], dso[4 * u + 3]);
       }
       fence_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(buf_full);
-      // use 2 it + 1 (dS) once dV^T consumed P
-      ok = mbar_wait(buf_empty, 0, g);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const uint32_t off = pb_row + ((((uint32_t)(wg & 1) * 4 + u) ^ rsw) << 4);
-        *reinterpret_cast<uint4*>(sPB + off) =
-            make_uint4(dpo[4 * u], dpo[4 * u + 1], dpo[4 * u + 2], dpo[4 * u + 3]);
-      }
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(buf_full);
+      if (lane == 0) mbar_arrive(ds_full);
       hh = hh_n;
       m = m_n;
       if (++m_n == p.n_qtiles) {
