@@ -1242,9 +1242,6 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
       const uint32_t p_addr = smem_u32(sP), ds_addr = smem_u32(sDS);
       bool ok = mbar_wait(kv_full, 0, g);
       if (ok) tc_fence_after();
-      int next_s = 0, next_p = 0, next_v = 0, next_k = 0;
-      int idle = 0;
-      uint64_t t_idle = 0;
       auto acc_mma = [&](uint32_t acc_t, uint32_t a_base, uint32_t b_base, bool first) {
 #pragma unroll
         for (int kk = 0; kk < 128 / 16; ++kk) {  // K = 128 query rows, 16 per MMA
@@ -1253,69 +1250,55 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
                   idAcc, (!first || kk > 0) ? 1u : 0u);
         }
       };
-      while (ok && next_k < NIT) {
-        // dV^T(it): frees dO(it) for the next tile's load -- first
-        if (next_v < next_p && mbar_test(p_full, next_v & 1)) {
-          tc_fence_after();
-          acc_mma(tmem + L::TM_DV, do_addr, p_addr, next_v == 0);
-          umma_commit(p_empty);
-          umma_commit(do_empty);
-          ++next_v;
-          idle = 0;
-          t_idle = 0;
-          continue;
-        }
-        if (next_k < next_v && mbar_test(ds_full, next_k & 1)) {
-          tc_fence_after();
-          acc_mma(tmem + L::TM_DK, q_addr + (next_k % L::QS) * L::QB, ds_addr, next_k == 0);
-          umma_commit(ds_empty);
-          umma_commit(&q_empty[next_k % L::QS]);
-          if (next_k + 1 == NIT) umma_commit(acc_done);
-          ++next_k;
-          idle = 0;
-          t_idle = 0;
-          continue;
-        }
-        if (next_p < next_s && (next_p == 0 || mbar_test(dp_free, (next_p - 1) & 1)) &&
-            mbar_test(do_full, next_p & 1)) {
-          tc_fence_after();
+      // Issue in the order the softmax produces work, each step a (suspending)
+      // wait: S(it+1) as soon as S(it) was copied out, dV(it) on P(it), dK(it) on
+      // dS(it), dP(it+1) once dP(it) was copied out and dO(it+1) landed.
+      auto issue_S = [&](int it) {
+        tc_fence_after();
+        const uint32_t qa = q_addr + (it % L::QS) * L::QB;
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t o = (kk >> 2) * L::BOX + (kk & 3) * 32;
-            umma_ss(tmem + L::TM_DP, make_sdesc_sw128(do_addr + o, 16, 1024), make_sdesc_sw128(v_addr + o, 16, 1024),
-                    idS, kk > 0 ? 1u : 0u);
-          }
-          umma_commit(dp_full);
-          ++next_p;
-          idle = 0;
-          t_idle = 0;
-          continue;
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t o = (kk >> 2) * L::BOX + (kk & 3) * 32;
+          umma_ss(tmem + L::TM_S, make_sdesc_sw128(qa + o, 16, 1024), make_sdesc_sw128(k_addr + o, 16, 1024), idS,
+                  kk > 0 ? 1u : 0u);
         }
-        if (next_s < NIT && (next_s == 0 || mbar_test(s_free, (next_s - 1) & 1)) &&
-            mbar_test(&q_full[next_s % L::QS], (next_s / L::QS) & 1)) {
-          tc_fence_after();
-          const uint32_t qa = q_addr + (next_s % L::QS) * L::QB;
+        umma_commit(s_full);
+      };
+      auto issue_dP = [&]() {
+        tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t o = (kk >> 2) * L::BOX + (kk & 3) * 32;
-            umma_ss(tmem + L::TM_S, make_sdesc_sw128(qa + o, 16, 1024), make_sdesc_sw128(k_addr + o, 16, 1024), idS,
-                    kk > 0 ? 1u : 0u);
-          }
-          umma_commit(s_full);
-          ++next_s;
-          idle = 0;
-          t_idle = 0;
-          continue;
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t o = (kk >> 2) * L::BOX + (kk & 3) * 32;
+          umma_ss(tmem + L::TM_DP, make_sdesc_sw128(do_addr + o, 16, 1024), make_sdesc_sw128(v_addr + o, 16, 1024),
+                  idS, kk > 0 ? 1u : 0u);
         }
-        if (++idle == 64) {
-          idle = 0;
-          const uint64_t now = global_timer_ns();
-          if (t_idle == 0) t_idle = now;
-          if (g.aborted()) ok = false;
-          else if (now - t_idle > g.timeout_ns) {
-            g.raise(kStatusTimeout);
-            ok = false;
-          }
+        umma_commit(dp_full);
+      };
+      if (ok) ok = mbar_wait(&q_full[0], 0, g);
+      if (ok) issue_S(0);
+      if (ok) ok = mbar_wait(do_full, 0, g);
+      if (ok) issue_dP();
+      for (int it = 0; ok && it < NIT; ++it) {
+        if (it + 1 < NIT) {
+          if (!(ok = mbar_wait(s_free, it & 1, g))) break;
+          if (!(ok = mbar_wait(&q_full[(it + 1) % L::QS], ((it + 1) / L::QS) & 1, g))) break;
+          issue_S(it + 1);
+        }
+        if (!(ok = mbar_wait(p_full, it & 1, g))) break;
+        tc_fence_after();
+        acc_mma(tmem + L::TM_DV, do_addr, p_addr, it == 0);
+        umma_commit(p_empty);
+        umma_commit(do_empty);
+        if (!(ok = mbar_wait(ds_full, it & 1, g))) break;
+        tc_fence_after();
+        acc_mma(tmem + L::TM_DK, q_addr + (it % L::QS) * L::QB, ds_addr, it == 0);
+        umma_commit(ds_empty);
+        umma_commit(&q_empty[it % L::QS]);
+        if (it + 1 == NIT) umma_commit(acc_done);
+        if (it + 1 < NIT) {
+          if (!(ok = mbar_wait(dp_free, it & 1, g))) break;
+          if (!(ok = mbar_wait(do_full, (it + 1) & 1, g))) break;
+          issue_dP();
         }
       }
       umma_commit(mma_idle);
