@@ -158,9 +158,14 @@ unsigned long long timeout_ns(unsigned ms) {
 template <int D, bool BF16>
 int launch_fwd_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const FwdParams& p,
                cudaStream_t stream) {
-  // persistent: one CTA per SM walks (head, query tile) items in a static round robin
+  // Large problems: persistent, one CTA per SM walking (head, query tile) items in a
+  // static snake order (the next item's loads and first MMAs overlap this one's
+  // epilogue).  Below about 12 items per SM the static order leaves SMs idle at the
+  // end, so each CTA then takes one item and the hardware balances (measured:
+  // B = 1, 2 at H16 S4096 one-item 25% faster; B = 4, 8 persistent 2-4% faster).
   const int n_items = p.B * p.Hq * p.n_qtiles;
-  const int grid = n_items < current_sm_count() ? n_items : current_sm_count();
+  const int sms = current_sm_count();
+  const int grid = (n_items >= 12 * sms) ? sms : n_items;
   coalibi_fwd_kernel<D, BF16><<<grid, FwdLayout<D>::THREADS, FwdLayout<D>::ALLOC, stream>>>(tq, tk, tv, p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
