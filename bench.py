@@ -44,7 +44,7 @@ CONFIGS = {
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of each
 # kernel at cfg2: one ncu capture at B=2 (profiles/<kernel>_kernel_cfg2_b2_ncu_full.txt)
 # scaled by 4 to the B=8 launch (traffic grows with the number of (b, h) units).
-NCU_TRAFFIC_CFG2 = {"fwd": 4 * 121.5e6, "bwd_a": 4 * 205.5e6, "bwd_b": 4 * 250.6e6, "bwd_delta": None}
+NCU_TRAFFIC_CFG2 = {"fwd": 4 * 116.0e6, "bwd_a": 4 * 206.0e6, "bwd_b": 4 * 253.4e6, "bwd_delta": None}
 
 
 def visible(S, causal):
@@ -378,9 +378,10 @@ def main():
     burst, sustained, hbm, peak_src = load_peaks()
     per_kernel_flops = {"fwd": 4.0 * D * E, "bwd_a": 6.0 * D * E, "bwd_b": 8.0 * D * E,
                         "bwd_delta": 0.0}
-    # MUFU ops per visible score: forward = tanh sigmoid + half of the exp2 (the other
-    # half runs as a polynomial on the FMA pipe); backward passes = tanh + exp2
-    per_kernel_mufu = {"fwd": 2.0 * E, "bwd_a": 2.0 * E, "bwd_b": 2.0 * E, "bwd_delta": 0.0}
+    # MUFU ops per visible score: tanh sigmoid + exp2, less the quarter of the exp2
+    # that the forward and the D=128 pass B run as a polynomial on the FMA pipe
+    mufu_b = 1.75 if D == 128 else 2.0
+    per_kernel_mufu = {"fwd": 1.75 * E, "bwd_a": 2.0 * E, "bwd_b": mufu_b * E, "bwd_delta": 0.0}
     dom = max(kern_ms, key=kern_ms.get)
     ach = per_kernel_flops[dom] / (kern_ms[dom] * 1e-3) / 1e12
     sm_mhz = clocks["sm_mhz"] if clocks else 1965.0
@@ -397,7 +398,7 @@ def main():
             "flops_per_launch": per_kernel_flops[dom],
             "note": "algorithmic FLOPs on causal-visible scores of the kernel's GEMMs "
                     "(fwd 4D, pass A 6D, pass B 8D per score) / mean CUDA-event duration in the timed region; "
-                    "second roofline: mufu_frac = MUFU ops per score (tanh + ex2 = 2 in every kernel) / (16 ops/clk/SM x 148 SMs x sampled clock)"}
+                    "second roofline: mufu_frac = MUFU ops per score (tanh + ex2 = 2, 1.75 where a quarter of the ex2 is a polynomial) / (16 ops/clk/SM x 148 SMs x sampled clock)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -1076,7 +1076,9 @@ __device__ __forceinline__ void bwd_b_phase_a(uint32_t* sreg, float* sg, uint32_
     zs = z.y - s.y;
     const float2 e = __ffma2_rn(make_float2(-slope2, -slope2), z,
                                 __ffma2_rn(x, make_float2(c_a, c_a), make_float2(-lse2, -lse2)));
-    float2 P = make_float2(ex2_approx(e.x), ex2_approx(e.y));
+    // A quarter of the exponentials on the FMA pipe relieves the MUFU unit,
+    // which also carries the tanh of every key.
+    float2 P = ((j2 & 3) == 3) ? exp2_poly2(e) : make_float2(ex2_approx(e.x), ex2_approx(e.y));
     if (MASK && key0 + j >= lim) P.x = 0.f;
     if (MASK && key0 + j + 1 >= lim) P.y = 0.f;
     sg[j] = s.x;
