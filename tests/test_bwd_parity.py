@@ -103,6 +103,28 @@ def test_backward_bench_shape_sampled(api):
             assert e <= GRAD_REL, f"(b={b}, h={h}) {name} relative error {e:.3e}"
 
 
+def test_backward_gqa_ragged_long_sampled(api):
+    """GQA (4 query heads per kv head), bf16, S = 4000 (ragged last tile): dQ of two
+    query heads and dK/dV of one kv head (its four query heads' contributions summed)
+    against the float32 oracle."""
+    from oracle import coalibi_oracle as orc
+    B, Hq, Hkv, S, D = 2, 32, 8, 4000, 128
+    q, k, v, do = make_inputs(B, Hq, Hkv, S, S, D, torch.bfloat16, seed=4)
+    _, dq, dk, dv = _run(api, q, k, v, do, True, 1.0 / math.sqrt(D))
+    sl = orc.api_slopes(Hq, 8.0, torch.bfloat16)
+    b, g = 1, 5
+    units = [(b, h) for h in range(4 * g, 4 * g + 4)]
+    res = orc.forward_sliced(q, k, v, sl, True, None, torch.float32, units=units, with_backward=True, do=do)
+    for h in (4 * g, 4 * g + 3):
+        e = rel_err(dq[b, h], res[(b, h)][3])
+        assert e <= GRAD_REL, f"(b={b}, h={h}) dq relative error {e:.3e}"
+    dk_ref = sum(res[u][4] for u in units)
+    dv_ref = sum(res[u][5] for u in units)
+    for name, x, r in (("dk", dk[b, g], dk_ref), ("dv", dv[b, g], dv_ref)):
+        e = rel_err(x, r)
+        assert e <= GRAD_REL, f"(b={b}, g={g}) {name} relative error {e:.3e}"
+
+
 def test_backward_deterministic(api):
     q, k, v, do = make_inputs(1, 4, 2, 700, 700, 128, torch.float16, seed=9)
     r1 = _run(api, q, k, v, do, True, 1 / math.sqrt(128))

@@ -108,6 +108,30 @@ def test_forward_bench_shape_sampled(api):
         assert ok, f"(b={b}, h={h}) O max-abs {err:.3e}"
 
 
+@pytest.mark.parametrize("shape", [
+    # B, Hq, Hkv, S, D, causal, dtype: each has at least 12 (head, query tile) items
+    # per SM, so the launch takes the persistent grid
+    (2, 32, 8, 4000, 128, True, torch.bfloat16),    # GQA, ragged last query tile
+    (16, 12, 12, 2048, 64, False, torch.float16),   # D = 64, non-causal
+])
+def test_forward_persistent_grid_sampled(api, shape):
+    """The persistent forward on GQA, ragged, bf16, D = 64 and non-causal problems;
+    the oracle checks a sample of (b, h) slices in float32."""
+    from oracle import coalibi_oracle as orc
+    B, Hq, Hkv, S, D, causal, dt = shape
+    q, k, v, _ = make_inputs(B, Hq, Hkv, S, S, D, dt, seed=3)
+    o = api.co_alibi_attention(q.cuda(), k.cuda(), v.cuda(), causal=causal).cpu()
+    sl = orc.api_slopes(Hq, 8.0, dt)
+    G = Hq // Hkv
+    for (b, h) in [(0, 0), (B - 1, Hq // 2 + 1), (B // 2, Hq - 1)]:
+        vs = v[b:b + 1, h // G:h // G + 1]
+        o_ref, _, _, it = orc.forward(q[b:b + 1, h:h + 1], k[b:b + 1, h // G:h // G + 1], vs, sl[h:h + 1],
+                                      causal, None, torch.float32, return_intermediates=True)
+        p_abs_v = (it["s"] @ vs.float().abs())[0, 0]
+        ok, err = check_o(o[b, h], o_ref[0, 0], dt, p_abs_v)
+        assert ok, f"(b={b}, h={h}) O max-abs {err:.3e}"
+
+
 def test_forward_deterministic(api):
     q, k, v, _ = make_inputs(1, 4, 4, 700, 700, 128, torch.float16, seed=5)
     a = api.co_alibi_attention(q.cuda(), k.cuda(), v.cuda())
