@@ -248,7 +248,7 @@ def main():
     from co_alibi_attn import co_alibi_attention
     import co_alibi_attn.co_alibi_attn as impl
 
-    from co_alibi_attn.sharding import shard_plan, sharded_attention
+    from co_alibi_attn.sharding import shard_plan, sharded_attention, shard_slopes
     B, Hq, Hkv, S, D, dtype, causal, std, fwd_only = cfg
     if args.scaling == "strong" and world > 1:
         # the batch's B*Hkv (b, kv head) units split into one contiguous block per rank
@@ -333,8 +333,11 @@ def main():
         outs_h += [torch.empty_like(q_h).pin_memory(), torch.empty_like(k_h).pin_memory(),
                    torch.empty_like(v_h).pin_memory()]
 
+    e2e_slopes = (shard_slopes(Hq, shard, 8.0, dtype, dev) if args.scaling == "strong" and world > 1 else None)
+
     def e2e_step():
-        co_alibi_attention_from_host(q_h, k_h, v_h, None if fwd_only else do_h, out=outs_h, device=dev, fn=attn)
+        co_alibi_attention_from_host(q_h, k_h, v_h, None if fwd_only else do_h, causal=causal, out=outs_h, device=dev,
+                                     slopes=e2e_slopes)
 
     e2e_ms = float("nan")
     if args.e2e_steps > 0:

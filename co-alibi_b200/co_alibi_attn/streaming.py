@@ -3,15 +3,17 @@ host<->device copies overlapped with the kernels.
 
 Every (batch, head) slice of the problem is independent (the reference kernels
 launch one program per (batch*head, block): ``co_alibi_attn/co_alibi_attn.py:40``
-and ``:83``), so the batch is cut into chunks of batch elements and pipelined
-over three CUDA streams: the copy-in of chunk c+1, the forward (and backward)
-of chunk c and the copy-out of chunk c-1 run at the same time, and the copies
-in the two PCIe directions overlap each other.  Results are identical to
+and ``:83``), so the batch is cut into chunks -- one batch element and a range
+of kv heads (with their query heads) each, contiguous in host memory -- and
+pipelined over three CUDA streams: the copy-in of chunk c+1, the forward (and
+backward) of chunk c and the copy-out of chunk c-1 run at the same time, and the
+copies in the two PCIe directions overlap each other.  Every chunk runs with the
+slopes of its global head indices, so results are identical to
 ``co_alibi_attention`` on the whole batch on the device.
 """
 import torch
 
-from .co_alibi_attn import co_alibi_attention
+from .co_alibi_attn import _api_slopes, _bwd, _check_inputs, _fwd
 
 __all__ = ["co_alibi_attention_from_host"]
 
@@ -39,21 +41,23 @@ def _check_host(name, t, dtype):
         raise ValueError(f"{name} has dtype {t.dtype}, expected {dtype}")
     if t.dim() != 4:
         raise ValueError(f"{name} must be [B, H, S, D], got shape {tuple(t.shape)}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
 
 
 def co_alibi_attention_from_host(q, k, v, do=None, causal=True, sm_scale=None, bias_max=8.0, out=None,
-                                 device=None, chunk=1, fn=None):
+                                 device=None, slopes=None, chunks=16):
     """Co-ALiBi attention of host tensors, streamed through one GPU.
 
     q: [B, Hq, Sq, D]; k, v: [B, Hkv, Skv, D]; ``do`` (optional): [B, Hq, Sq, D],
-    the gradient of the output.  All CPU tensors of one dtype, ideally in pinned
-    memory (pageable memory works but its copies do not overlap).  Returns host
-    tensors ``(o,)`` or, with ``do``, ``(o, dq, dk, dv)``; when ``out`` is given
-    (a tuple of the same shapes, pinned CPU tensors) the results are written
-    there.  ``chunk`` batch elements go through the device at a time.  ``fn``
-    (optional) replaces the per-chunk attention call: ``fn(q, k, v) -> o`` on
-    device tensors (for instance a head shard with global-head slopes).  The
-    call returns once the results are in host memory.
+    the gradient of the output.  All contiguous CPU tensors of one dtype, ideally
+    in pinned memory (pageable memory works but its copies do not overlap).
+    Returns host tensors ``(o,)`` or, with ``do``, ``(o, dq, dk, dv)``; when
+    ``out`` is given (a tuple of the same shapes, CPU tensors) the results are
+    written there.  ``slopes`` (optional, [Hq]) replaces the slope table of
+    ``co_alibi_attention`` (for instance the global-head slopes of a head shard).
+    The batch goes through the device in about ``chunks`` pieces.  The call
+    returns once the results are in host memory.
     """
     _check_host("q", q, q.dtype)
     _check_host("k", k, q.dtype)
@@ -62,11 +66,14 @@ def co_alibi_attention_from_host(q, k, v, do=None, causal=True, sm_scale=None, b
         _check_host("do", do, q.dtype)
         if do.shape != q.shape:
             raise ValueError(f"do has shape {tuple(do.shape)}, expected {tuple(q.shape)}")
-    B = q.shape[0]
-    if k.shape[0] != B or v.shape != k.shape or k.shape[-1] != q.shape[-1]:
+    B, Hq = q.shape[0], q.shape[1]
+    Hkv = k.shape[1]
+    if k.shape[0] != B or v.shape != k.shape or k.shape[-1] != q.shape[-1] or Hq % Hkv != 0:
         raise ValueError(f"inconsistent shapes q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)}")
-    if chunk < 1:
-        raise ValueError("chunk must be >= 1")
+    if chunks < 1:
+        raise ValueError("chunks must be >= 1")
+    if slopes is not None and tuple(slopes.shape) != (Hq,):
+        raise ValueError(f"slopes must have shape ({Hq},)")
     shapes = [q.shape] if do is None else [q.shape, q.shape, k.shape, v.shape]
     if out is None:
         pin = q.is_pinned()
@@ -74,55 +81,68 @@ def co_alibi_attention_from_host(q, k, v, do=None, causal=True, sm_scale=None, b
     else:
         out = tuple(out)
         if len(out) != len(shapes) or any(o.shape != s or o.dtype != q.dtype or o.device.type != "cpu"
-                                          for o, s in zip(out, shapes)):
-            raise ValueError("out must hold CPU tensors of the result shapes and dtype")
+                                          or not o.is_contiguous() for o, s in zip(out, shapes)):
+            raise ValueError("out must hold contiguous CPU tensors of the result shapes and dtype")
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    if fn is None:
-        def fn(q_, k_, v_):
-            return co_alibi_attention(q_, k_, v_, causal, sm_scale, bias_max)
+    if sm_scale is None:
+        sm_scale = 1.0 / (q.shape[-1] ** 0.5)
+    G = Hq // Hkv
+    # chunk = (batch element, kv heads [g0, g1)); kv heads per chunk so that B * pieces ~ chunks
+    per_b = max(1, min(Hkv, -(-chunks // B)))
+    gstep = -(-Hkv // per_b)
+    units = [(b, g0, min(Hkv, g0 + gstep)) for b in range(B) for g0 in range(0, Hkv, gstep)]
+    n = len(units)
     ins = [q, k, v] + ([] if do is None else [do])
-    n = (B + chunk - 1) // chunk
     with torch.cuda.device(dev):
+        sl = (_api_slopes(Hq, bias_max, q.dtype, dev) if slopes is None
+              else slopes.to(device=dev).contiguous())
         caller = torch.cuda.current_stream()
         s_in, s_comp, s_out = _stream_triple(dev)
         for s in (s_in, s_comp, s_out):
             s.wait_stream(caller)
         # two device slots per input: chunk c+2 overwrites chunk c's inputs once its compute finished
-        slots = [[torch.empty((min(chunk, B),) + tuple(t.shape[1:]), dtype=t.dtype, device=dev) for t in ins]
-                 for _ in range(min(2, n))]
+        sizes = [(1, gstep * G) + tuple(q.shape[2:]), (1, gstep) + tuple(k.shape[2:]),
+                 (1, gstep) + tuple(v.shape[2:]), (1, gstep * G) + tuple(q.shape[2:])]
+        slots = [[torch.empty(sz, dtype=q.dtype, device=dev) for sz in sizes[:len(ins)]] for _ in range(min(2, n))]
         comp_done = []
         keep = []
-        for c in range(n):
-            b0, b1 = c * chunk, min(B, (c + 1) * chunk)
-            buf = [t[: b1 - b0] for t in slots[c % 2]]
+        for c, (b, g0, g1) in enumerate(units):
+            h0, h1 = g0 * G, g1 * G
+            hosts = [q[b:b + 1, h0:h1], k[b:b + 1, g0:g1], v[b:b + 1, g0:g1]]
+            if do is not None:
+                hosts.append(do[b:b + 1, h0:h1])
+            buf = [t[:, : h.shape[1]] for t, h in zip(slots[c % 2], hosts)]
             with torch.cuda.stream(s_in):
                 if c >= 2:
                     s_in.wait_event(comp_done[c - 2])
-                for d, h in zip(buf, ins):
-                    d.copy_(h[b0:b1], non_blocking=True)
+                for d, h in zip(buf, hosts):
+                    d.copy_(h, non_blocking=True)
                 h2d = torch.cuda.Event()
                 h2d.record(s_in)
             with torch.cuda.stream(s_comp):
                 s_comp.wait_event(h2d)
+                # the kernels the autograd Function runs, called directly (no graph per chunk)
+                slc = sl[h0:h1]
+                if c == 0:
+                    _check_inputs(buf[0], buf[1], buf[2], slc)
+                o, lse, rowsig = _fwd(buf[0], buf[1], buf[2], slc, causal, sm_scale)
                 if do is None:
-                    with torch.no_grad():
-                        res = (fn(buf[0], buf[1], buf[2]),)
+                    res = (o,)
                 else:
-                    qq, kk, vv = (t.detach().requires_grad_(True) for t in buf[:3])
-                    o = fn(qq, kk, vv)
-                    o.backward(buf[3])
-                    res = (o.detach(), qq.grad, kk.grad, vv.grad)
+                    res = (o,) + tuple(_bwd(buf[0], buf[1], buf[2], o, buf[3], lse, rowsig, slc, causal, sm_scale))
                 ev = torch.cuda.Event()
                 ev.record(s_comp)
                 comp_done.append(ev)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(ev)
-                for h, d in zip(out, res):
+                dsts = [out[0][b:b + 1, h0:h1]]
+                if do is not None:
+                    dsts += [out[1][b:b + 1, h0:h1], out[2][b:b + 1, g0:g1], out[3][b:b + 1, g0:g1]]
+                for h, d in zip(dsts, res):
                     d.record_stream(s_out)
-                    h[b0:b1].copy_(d, non_blocking=True)
+                    h.copy_(d, non_blocking=True)
             keep.append(res)
-        caller.wait_stream(s_out)
-        for s in (s_in, s_comp):
+        for s in (s_in, s_comp, s_out):
             caller.wait_stream(s)
         s_out.synchronize()
     return out
