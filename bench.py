@@ -1,7 +1,7 @@
 """Benchmark of the Co-ALiBi hot path (forward + backward) on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config cfg2|cfg3|cfg4] [--scaling weak|strong]
+                    [--config cfg2|cfg3|cfg4|cfg5] [--scaling weak|strong]
 
 One step = co_alibi_attention(q, k, v, causal) forward and backward over one
 batch of the named configuration (default cfg2: B=8, H=16, S=4096, D=128, fp16,
@@ -13,6 +13,10 @@ steps.  N>1 runs one process per GPU under torchrun; every rank runs its own
 batch; "strong": the batch's B*Hkv units are split across ranks).  Time is taken
 with CUDA events on the launching stream, between a barrier and a synchronize,
 and the maximum over ranks is reported.
+
+``--config cfg5`` instead times one data-parallel training step of the small
+Co-ALiBi GPT (co_alibi_gpt: 12 layers, d_model 768, 12 heads of D=64, seq 1024,
+batch 32 per GPU, bf16, DDP over NCCL, AdamW) and reports tokens per second.
 
 Prints ONE JSON line (rank 0).  ``--impl reference`` times the reference
 algorithm's CPU path (the oracle restatement of model.py, on all host cores)
@@ -190,10 +194,141 @@ def run_reference_arm(args, cfg, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_gpt(args, world, rank, local_rank, dev):
+    """cfg5: one data-parallel training step of the small Co-ALiBi GPT per step
+    (forward, backward with the NCCL gradient all-reduce of DDP, AdamW update);
+    value = tokens per second over all ranks."""
+    import torch.distributed as dist
+    import co_alibi_attn
+    import co_alibi_attn.co_alibi_attn as impl
+    from co_alibi_gpt import GPTConfig, build, make_tokens, train_step
+    cfg = GPTConfig()
+    batch = args.batch or 32
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    model, opt = build(cfg, dev, seed=0, ddp=world > 1)
+    core = model.module if world > 1 else model
+    tok_h = make_tokens(cfg, batch, seed=1000 + rank).pin_memory()
+    tok = tok_h.to(dev)
+    for _ in range(args.warmup):
+        train_step(model, opt, tok)
+    torch.cuda.synchronize()
+    assert co_alibi_attn.device_status(reset=True) == 0, "kernel-side error during warmup"
+
+    sampler = ClockSampler(physical_gpu_index(local_rank))
+    sampler.start()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        train_step(model, opt, tok)
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = t.item()
+    tokens_rank = batch * cfg.seq_len
+    value = world * tokens_rank / (ms_max * 1e-3)
+    flops_rank = core.flops_per_token() * tokens_rank
+    burst, sustained, hbm, peak_src = load_peaks()
+    achieved = flops_rank / (ms_max * 1e-3) / 1e12
+
+    # attention kernels inside a step (CUDA events around each launch, separate short pass)
+    impl.kernel_events = {}
+    for _ in range(3):
+        train_step(model, opt, tok)
+    torch.cuda.synchronize()
+    attn_ms = sum(a.elapsed_time(b) for v in impl.kernel_events.values() for a, b in v) / 3
+    impl.kernel_events = None
+    attn_flops = cfg.n_layer * 14 * cfg.d_model * (cfg.seq_len + 1) / 2 * tokens_rank
+
+    # e2e: token ids from pinned host memory every step, the loss read back every step
+    loss_h = torch.empty((), dtype=torch.float32).pin_memory()
+    tok_d = torch.empty_like(tok)
+    barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    n_e2e = max(1, args.e2e_steps)
+    for _ in range(n_e2e):
+        tok_d.copy_(tok_h, non_blocking=True)
+        loss = train_step(model, opt, tok_d)
+        loss_h.copy_(loss.float(), non_blocking=True)
+    f1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([f0.elapsed_time(f1) / n_e2e], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = t.item()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = gpt_cpu_sample(cfg)
+    if rank == 0:
+        line = {
+            "metric": metric_name("cfg5"), "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (token ids uniform over the vocabulary, weights N(0, 0.02))",
+            "config": {"workload": f"cfg5: Co-ALiBi GPT training step, {cfg.n_layer} layers, d_model {cfg.d_model}, "
+                                   f"{cfg.n_head} heads (D=64), MLP 4x GELU, vocab {cfg.vocab}, seq {cfg.seq_len}, "
+                                   f"batch {batch} per GPU, bf16 weights, AdamW",
+                       "global_batch": world * batch, "seq_len": cfg.seq_len,
+                       "parallelism": f"data-parallel x{world} (DDP, NCCL all-reduce of bf16 gradients)",
+                       "l2": "weights, activations and optimizer state exceed the 126 MB L2"},
+            "model_tflops_per_gpu": round(achieved, 2),
+            "attention": {"ms_per_step": round(attn_ms, 3), "share": round(attn_ms / ms_max, 4),
+                          "tflops": round(attn_flops / (attn_ms * 1e-3) / 1e12, 2) if attn_ms > 0 else None},
+            "roofline": {"bound": "tensor", "kernel": "whole training step (GEMMs + Co-ALiBi attention)",
+                         "achieved": round(achieved, 2), "peak": sustained, "unit": "TFLOP/s",
+                         "frac": round(achieved / sustained, 4),
+                         "peak_source": f"{peak_src} bf16_tflops_sustained", "traffic": None,
+                         "note": "6 x matmul parameters per token + causal attention GEMMs, per GPU"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(world * tokens_rank / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                    "ms_per_step": round(e2e_ms, 3),
+                    "h2d_bytes_per_step": tok_h.numel() * tok_h.element_size(), "d2h_bytes_per_step": 4},
+            "gpu_launches": 4 * cfg.n_layer * args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def gpt_cpu_sample(cfg):
+    """The same GPT, float32 on the host cores, the attention from the oracle
+    (the reference's own maths restated): one sequence forward + backward."""
+    from co_alibi_gpt import build, make_tokens
+    from oracle import coalibi_oracle as orc
+    torch.set_num_threads(os.cpu_count() or 1)
+
+    def attn(q, k, v, causal=True, bias_max=8.0):
+        sl = orc.api_slopes(q.shape[1], bias_max, q.dtype)
+        return orc.forward(q, k, v, sl, causal, None, torch.float32)[0]
+
+    model, _ = build(cfg, "cpu", seed=0, dtype=torch.float32, attn_fn=attn)
+    tok = make_tokens(cfg, 1, seed=7)
+    model(tok[:, :-1], targets=tok[:, 1:]).backward()
+    model.zero_grad(set_to_none=True)
+    t0 = time.perf_counter()
+    model(tok[:, :-1], targets=tok[:, 1:]).backward()
+    sec = time.perf_counter() - t0
+    return {"value": round(cfg.seq_len / sec, 1), "unit": "tokens/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"one sequence of {cfg.seq_len} tokens, forward + backward, float32, "
+                                      "attention from the oracle (model.py maths)", "seconds_per_sample": round(sec, 3)}
+
+
 def metric_name(config):
     return {"cfg2": "fwd+bwd TFLOP/s (algorithmic causal), B8 H16 S4096 D128 fp16 causal",
             "cfg3": "fwd+bwd TFLOP/s (algorithmic causal), GQA B4 Hq32 Hkv8 S8192 D128 bf16 causal",
-            "cfg4": "fwd TFLOP/s, B16 H12 S2048 D64 fp16 non-causal"}[config]
+            "cfg4": "fwd TFLOP/s, B16 H12 S2048 D64 fp16 non-causal",
+            "cfg5": "Co-ALiBi GPT training step tokens/s (12 layers, d768, 12 heads D64, seq 1024, batch 32 per GPU)"}[config]
 
 
 def config_dict(args, cfg):
@@ -217,7 +352,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS) + ["cfg5"])
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--batch", type=int, default=None,
@@ -225,9 +360,17 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    cfg = CONFIGS[args.config]
-    if args.batch:
-        cfg = (args.batch,) + cfg[1:]
+    if args.config == "cfg5":
+        if args.impl == "reference":
+            if int(os.environ.get("RANK", "0")) == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference ships no model code; cfg5 is "
+                                  "a caller built here"}), flush=True)
+            return
+        cfg = None
+    else:
+        cfg = CONFIGS[args.config]
+        if args.batch:
+            cfg = (args.batch,) + cfg[1:]
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -255,6 +398,13 @@ def main():
         finally:
             os.dup2(saved_fd, 1)
             os.close(saved_fd)
+
+    if args.config == "cfg5":
+        run_gpt(args, world, rank, local_rank, dev)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     import co_alibi_attn
     from co_alibi_attn import co_alibi_attention
