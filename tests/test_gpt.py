@@ -73,7 +73,8 @@ def _ddp_worker(rank, world, port, out):
         tok = make_tokens(cfg, 4, seed=3)[2 * rank:2 * rank + 2]  # each rank: half of the batch
         model(tok[:, :-1], targets=tok[:, 1:]).backward()
         if rank == 0:
-            out.put({n: p.grad.clone() for n, p in model.module.named_parameters()})
+            # numpy copies travel by value (tensors would be shared-memory handles that die with the worker)
+            out.put({n: p.grad.detach().numpy().copy() for n, p in model.module.named_parameters()})
     finally:
         dist.destroy_process_group()
 
@@ -97,7 +98,7 @@ def test_gpt_ddp_gloo_averages_gradients():
     tok = make_tokens(cfg, 4, seed=3)
     model(tok[:, :-1], targets=tok[:, 1:]).backward()
     for n, p in model.named_parameters():
-        assert torch.allclose(got[n], p.grad, rtol=1e-4, atol=1e-6), n
+        assert torch.allclose(torch.from_numpy(got[n]), p.grad, rtol=1e-4, atol=1e-6), n
 
 
 @pytest.mark.gpu
