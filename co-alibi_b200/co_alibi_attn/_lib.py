@@ -39,7 +39,7 @@ class CoalibiBwdArgs(ctypes.Structure):
     ]
 
 
-EXPORTS = ("coalibi_fwd", "coalibi_bwd", "coalibi_bwd_phases", "coalibi_bwd_noalloc",
+EXPORTS = ("coalibi_fwd", "coalibi_fwd_decode", "coalibi_fwd_decode_workspace_bytes", "coalibi_bwd", "coalibi_bwd_phases", "coalibi_bwd_noalloc",
            "coalibi_bwd_workspace_bytes", "coalibi_selftest_wait_timeout", "coalibi_strerror",
            "coalibi_abi_version", "coalibi_last_error")
 
@@ -63,6 +63,10 @@ def load():
             lib = ctypes.CDLL(LIB_PATH)
             lib.coalibi_fwd.argtypes = [ctypes.POINTER(CoalibiFwdArgs), c_void_p]
             lib.coalibi_fwd.restype = c_int
+            lib.coalibi_fwd_decode.argtypes = [ctypes.POINTER(CoalibiFwdArgs), c_void_p, c_size_t, c_void_p]
+            lib.coalibi_fwd_decode.restype = c_int
+            lib.coalibi_fwd_decode_workspace_bytes.argtypes = [c_int] * 6
+            lib.coalibi_fwd_decode_workspace_bytes.restype = c_size_t
             lib.coalibi_bwd.argtypes = [ctypes.POINTER(CoalibiBwdArgs), c_void_p]
             lib.coalibi_bwd.restype = c_int
             lib.coalibi_bwd_phases.argtypes = [ctypes.POINTER(CoalibiBwdArgs), c_int, c_void_p]

@@ -100,7 +100,14 @@ def _check_inputs(q, k, v, slopes):
         raise TypeError(f"co_alibi_attn: slopes must be float16/bfloat16/float32, got {slopes.dtype}")
 
 
-def _fwd(q, k, v, slopes, causal, sm_scale):
+# Sq limit of coalibi_fwd_decode (COALIBI_DECODE_MAX_SQ in coalibi.h)
+DECODE_MAX_SQ = 16
+
+
+def _fwd(q, k, v, slopes, causal, sm_scale, decode=False):
+    """Forward kernels: coalibi_fwd, or with ``decode`` (Sq <= DECODE_MAX_SQ) the
+    split-over-keys coalibi_fwd_decode.  The public API uses coalibi_fwd at every
+    Sq: at the measured decode shapes it is still the faster of the two."""
     B, Hq, Sq, D = q.shape
     Hkv, Skv = k.shape[1], k.shape[2]
     o = torch.empty_like(q)
@@ -117,7 +124,15 @@ def _fwd(q, k, v, slopes, causal, sm_scale):
     if rec is not None:
         e0, e1 = _ev(), _ev()
         e0.record()
-    _lib.check(_lib.load().coalibi_fwd(a, stream), "coalibi_fwd")
+    lib = _lib.load()
+    if decode:
+        if Sq > DECODE_MAX_SQ:
+            raise ValueError(f"co_alibi_attn: the decode forward takes Sq <= {DECODE_MAX_SQ}, got {Sq}")
+        nbytes = lib.coalibi_fwd_decode_workspace_bytes(B, Hq, Hkv, Sq, Skv, D)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+        _lib.check(lib.coalibi_fwd_decode(a, ws.data_ptr(), nbytes, stream), "coalibi_fwd_decode")
+    else:
+        _lib.check(lib.coalibi_fwd(a, stream), "coalibi_fwd")
     if rec is not None:
         e1.record()
         rec.setdefault("fwd", []).append((e0, e1))

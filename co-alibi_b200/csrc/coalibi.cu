@@ -12,6 +12,7 @@
 
 #include "coalibi.h"
 #include "fwd.cuh"
+#include "decode.cuh"
 #include "bwd.cuh"
 
 namespace coalibi {
@@ -123,6 +124,10 @@ int device_setup(const void* ptr) {
     ok &= set_smem(coalibi_fwd_kernel<128, true>, FwdLayout<128>::ALLOC);
     ok &= set_smem(coalibi_fwd_kernel<64, false>, FwdLayout<64>::ALLOC);
     ok &= set_smem(coalibi_fwd_kernel<64, true>, FwdLayout<64>::ALLOC);
+    ok &= set_smem(coalibi_decode_partial_kernel<128, false>, DecodeSmem<128>::BYTES);
+    ok &= set_smem(coalibi_decode_partial_kernel<128, true>, DecodeSmem<128>::BYTES);
+    ok &= set_smem(coalibi_decode_partial_kernel<64, false>, DecodeSmem<64>::BYTES);
+    ok &= set_smem(coalibi_decode_partial_kernel<64, true>, DecodeSmem<64>::BYTES);
     ok &= bwd_set_smem_attributes();
     st.status = ok ? COALIBI_OK : COALIBI_ERR_LAUNCH;
   });
@@ -250,6 +255,70 @@ extern "C" int coalibi_fwd(const CoalibiFwdArgs* a, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (a->D == 128) return bf16 ? launch_fwd<128, true>(tq, tk, tv, p, s) : launch_fwd<128, false>(tq, tk, tv, p, s);
   return bf16 ? launch_fwd<64, true>(tq, tk, tv, p, s) : launch_fwd<64, false>(tq, tk, tv, p, s);
+}
+
+namespace coalibi {
+namespace {
+template <int D, bool BF16>
+int launch_decode(const DecodeParams& p, cudaStream_t stream) {
+  const dim3 grid_p(p.B * p.Hkv, p.n_chunks, p.n_rgroups);
+  coalibi_decode_partial_kernel<D, BF16><<<grid_p, kDecodeBlock, DecodeSmem<D>::BYTES, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) {
+    coalibi_decode_combine_kernel<D, BF16><<<p.B * p.Hq * p.Sq, D, 0, stream>>>(p);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) {
+    snprintf(g_last_error, sizeof(g_last_error), "decode launch: %s", cudaGetErrorString(e));
+    return COALIBI_ERR_LAUNCH;
+  }
+  return COALIBI_OK;
+}
+}  // namespace
+}  // namespace coalibi
+
+extern "C" size_t coalibi_fwd_decode_workspace_bytes(int B, int Hq, int Hkv, int Sq, int Skv, int D) {
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || Skv <= 0 || Hq % Hkv != 0 || Sq > kDecodeMaxSq) return 0;
+  if (D != 64 && D != 128) return 0;
+  return D == 128 ? decode_plan<128>(B, Hq, Hkv, Sq, Skv).bytes : decode_plan<64>(B, Hq, Hkv, Sq, Skv).bytes;
+}
+
+extern "C" int coalibi_fwd_decode(const CoalibiFwdArgs* a, void* workspace, size_t workspace_bytes, void* stream) {
+  if (a == nullptr) return COALIBI_ERR_NULL_POINTER;
+  if (!a->q || !a->k || !a->v || !a->o || !a->lse || !a->rowsig || !a->slopes) return COALIBI_ERR_NULL_POINTER;
+  int rc = check_common(a->B, a->Hq, a->Hkv, a->Sq, a->Skv, a->D, a->dtype, a->slopes_dtype);
+  if (rc) return rc;
+  if (a->Sq > kDecodeMaxSq) return COALIBI_ERR_SHAPE;
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o)) return COALIBI_ERR_ALIGNMENT;
+  const size_t need = coalibi_fwd_decode_workspace_bytes(a->B, a->Hq, a->Hkv, a->Sq, a->Skv, a->D);
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)) return COALIBI_ERR_WORKSPACE;
+  if ((rc = device_setup(a->q))) return rc;
+  DecodeParams p{};
+  p.q = a->q;
+  p.k = a->k;
+  p.v = a->v;
+  p.slopes = a->slopes;
+  p.o = a->o;
+  p.lse = a->lse;
+  p.rowsig = a->rowsig;
+  p.ws = static_cast<float*>(workspace);
+  p.B = a->B;
+  p.Hq = a->Hq;
+  p.Hkv = a->Hkv;
+  p.Sq = a->Sq;
+  p.Skv = a->Skv;
+  p.slopes_dtype = a->slopes_dtype;
+  p.causal = a->causal ? 1 : 0;
+  p.sm_scale = a->sm_scale;
+  const DecodePlan pl = a->D == 128 ? decode_plan<128>(a->B, a->Hq, a->Hkv, a->Sq, a->Skv)
+                                    : decode_plan<64>(a->B, a->Hq, a->Hkv, a->Sq, a->Skv);
+  p.n_chunks = pl.n_chunks;
+  p.chunk_keys = pl.chunk_keys;
+  p.n_rgroups = pl.n_rgroups;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool bf16 = a->dtype == COALIBI_BF16;
+  if (a->D == 128) return bf16 ? launch_decode<128, true>(p, s) : launch_decode<128, false>(p, s);
+  return bf16 ? launch_decode<64, true>(p, s) : launch_decode<64, false>(p, s);
 }
 
 extern "C" size_t coalibi_bwd_workspace_bytes(int B, int Hq, int Hkv, int Sq, int Skv, int D) {

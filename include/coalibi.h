@@ -75,6 +75,19 @@ typedef struct CoalibiFwdArgs {
 
 int coalibi_fwd(const CoalibiFwdArgs* args, void* stream);
 
+/* Forward for few query rows (Sq <= COALIBI_DECODE_MAX_SQ, e.g. one new token
+ * against a long key/value sequence): the same arguments, mask semantics and
+ * results (o, lse, rowsig) as coalibi_fwd, for the shapes the reference forward
+ * launches with a nearly empty query block (co_alibi_attn/co_alibi_attn.py:44-57).
+ * The keys are split into chunks reduced by separate CTAs on CUDA cores and merged
+ * exactly: the sigmoid totals of the chunks to the right shift each chunk's
+ * logits.  workspace: device scratch of at least coalibi_fwd_decode_workspace_bytes()
+ * bytes, 16-byte aligned; contents on entry do not matter.  Sq above the limit
+ * returns COALIBI_ERR_SHAPE. */
+#define COALIBI_DECODE_MAX_SQ 16
+size_t coalibi_fwd_decode_workspace_bytes(int B, int Hq, int Hkv, int Sq, int Skv, int D);
+int coalibi_fwd_decode(const CoalibiFwdArgs* args, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Backward.  Replaces co_alibi_attn/co_alibi_attn.py:73-135 (CoALIBIAttention.backward,
  * including the dk/dv partial-buffer reduction at :132-133 and, for GQA, the group
  * sum autograd performs through repeat_interleave at :145-146) and the kernel
