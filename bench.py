@@ -301,6 +301,117 @@ def run_gpt(args, world, rank, local_rank, dev):
         print(json.dumps(line), flush=True)
 
 
+def run_decode(args, world, rank, local_rank, dev):
+    """decode: one new query row per (batch, head) against a 32,768-key cache
+    (B=8, Hq=32, Hkv=8, D=128, bf16, no mask) through co_alibi_attention, which
+    takes the split-over-keys decode kernels for Sq <= 16.  value = query rows
+    (generated tokens x heads / heads = tokens) per second over all ranks."""
+    import torch.distributed as dist
+    import co_alibi_attn
+    from co_alibi_attn import co_alibi_attention
+    import co_alibi_attn.co_alibi_attn as impl
+    B, Hq, Hkv, Sq, Skv, D, dt = (args.batch or 8), 32, 8, 1, 32768, 128, torch.bfloat16
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    g = torch.Generator().manual_seed(2000 + rank)
+    q_h = torch.randn(B, Hq, Sq, D, generator=g).to(dt).pin_memory()
+    k = torch.randn(B, Hkv, Skv, D, generator=g).to(dt).to(dev)
+    v = torch.randn(B, Hkv, Skv, D, generator=g).to(dt).to(dev)
+    q = q_h.to(dev)
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            co_alibi_attention(q, k, v, causal=False)
+    torch.cuda.synchronize()
+    assert co_alibi_attn.device_status(reset=True) == 0, "kernel-side error during warmup"
+    # K, V (2 x 1 GiB) exceed the L2: every call reads them from HBM
+    sampler = ClockSampler(physical_gpu_index(local_rank))
+    sampler.start()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.no_grad():
+        e0.record()
+        for _ in range(args.steps):
+            co_alibi_attention(q, k, v, causal=False)
+        e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = t.item()
+    bytes_call = (k.numel() + v.numel() + 2 * q.numel()) * 2
+    burst, sustained, hbm, peak_src = load_peaks()
+    gbs = bytes_call / (ms_max * 1e-3) / 1e9
+    # decode partial kernel alone (CUDA events around the launch pair)
+    impl.kernel_events = {}
+    with torch.no_grad():
+        for _ in range(5):
+            co_alibi_attention(q, k, v, causal=False)
+    torch.cuda.synchronize()
+    kms = sum(a.elapsed_time(b) for a, b in impl.kernel_events.get("fwd", [])) / 5
+    impl.kernel_events = None
+    # e2e: the new query rows from pinned host memory, the output read back, every call
+    o_h = torch.empty_like(q_h).pin_memory()
+    qd = torch.empty_like(q)
+    barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_e2e = max(1, args.e2e_steps)
+    with torch.no_grad():
+        f0.record()
+        for _ in range(n_e2e):
+            qd.copy_(q_h, non_blocking=True)
+            o = co_alibi_attention(qd, k, v, causal=False)
+            o_h.copy_(o, non_blocking=True)
+        f1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([f0.elapsed_time(f1) / n_e2e], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = t.item()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import coalibi_oracle as orc
+        torch.set_num_threads(os.cpu_count() or 1)
+        sl = orc.api_slopes(Hq, 8.0, torch.float32)[:1]
+        qs, ks, vs = q_h[:1, :1].float(), k[:1, :1].float().cpu(), v[:1, :1].float().cpu()
+        orc.forward(qs, ks, vs, sl, False, None, torch.float32)
+        t0 = time.perf_counter()
+        for _ in range(5):
+            orc.forward(qs, ks, vs, sl, False, None, torch.float32)
+        sec = (time.perf_counter() - t0) / 5
+        cpu = {"value": round(1.0 / sec, 1), "unit": "query rows/s", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"oracle (model.py maths) fp32, one query row of one head against {Skv} keys, mean of 5",
+               "seconds_per_sample": round(sec, 6)}
+    if rank == 0:
+        rows = B * Hq * Sq
+        line = {
+            "metric": metric_name("decode"), "value": round(world * rows / (ms_max * 1e-3), 1), "unit": "query rows/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"decode: co_alibi_attention fwd, B={B} Hq={Hq} Hkv={Hkv} Sq={Sq} Skv={Skv} D={D} "
+                                   "bf16, no mask (one new token per sequence against the key/value cache)",
+                       "global_batch": world * B, "seq_len": Skv, "parallelism": f"independent replicas x{world}",
+                       "l2": "K and V (2 GiB) exceed the 126 MB L2; no flush needed"},
+            "kv_read_gbs": round(gbs, 1),
+            "roofline": {"bound": "hbm", "kernel": "decode (partial + combine)", "achieved": round(gbs, 1),
+                         "peak": hbm, "unit": "GB/s", "frac": round(gbs / hbm, 4), "peak_source": f"{peak_src} hbm_gbs",
+                         "traffic": None, "kernel_ms": round(kms, 4),
+                         "note": "K + V + Q + O bytes per call / CUDA-event time of the call"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(world * rows / (e2e_ms * 1e-3), 1), "unit": "query rows/s", "ms_per_step": round(e2e_ms, 4),
+                    "h2d_bytes_per_step": q_h.numel() * 2, "d2h_bytes_per_step": o_h.numel() * 2},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+
+
 def gpt_cpu_sample(cfg):
     """The same GPT, float32 on the host cores, the attention from the oracle
     (the reference's own maths restated): one sequence forward + backward."""
@@ -328,7 +439,8 @@ def metric_name(config):
     return {"cfg2": "fwd+bwd TFLOP/s (algorithmic causal), B8 H16 S4096 D128 fp16 causal",
             "cfg3": "fwd+bwd TFLOP/s (algorithmic causal), GQA B4 Hq32 Hkv8 S8192 D128 bf16 causal",
             "cfg4": "fwd TFLOP/s, B16 H12 S2048 D64 fp16 non-causal",
-            "cfg5": "Co-ALiBi GPT training step tokens/s (12 layers, d768, 12 heads D64, seq 1024, batch 32 per GPU)"}[config]
+            "cfg5": "Co-ALiBi GPT training step tokens/s (12 layers, d768, 12 heads D64, seq 1024, batch 32 per GPU)",
+            "decode": "decode query rows/s, B8 Hq32 Hkv8 Sq1 Skv32768 D128 bf16"}[config]
 
 
 def config_dict(args, cfg):
@@ -352,7 +464,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS) + ["cfg5"])
+    ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS) + ["cfg5", "decode"])
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--batch", type=int, default=None,
@@ -360,11 +472,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    if args.config == "cfg5":
+    if args.config in ("cfg5", "decode"):
         if args.impl == "reference":
             if int(os.environ.get("RANK", "0")) == 0:
-                print(json.dumps({"impl": "reference", "unavailable": "the reference ships no model code; cfg5 is "
-                                  "a caller built here"}), flush=True)
+                why = ("the reference ships no model code; cfg5 is a caller built here" if args.config == "cfg5" else
+                       "the decode line is an addition of this build; the reference arm is the default config's")
+                print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
             return
         cfg = None
     else:
@@ -399,8 +512,8 @@ def main():
             os.dup2(saved_fd, 1)
             os.close(saved_fd)
 
-    if args.config == "cfg5":
-        run_gpt(args, world, rank, local_rank, dev)
+    if args.config in ("cfg5", "decode"):
+        (run_gpt if args.config == "cfg5" else run_decode)(args, world, rank, local_rank, dev)
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()

@@ -124,10 +124,10 @@ int device_setup(const void* ptr) {
     ok &= set_smem(coalibi_fwd_kernel<128, true>, FwdLayout<128>::ALLOC);
     ok &= set_smem(coalibi_fwd_kernel<64, false>, FwdLayout<64>::ALLOC);
     ok &= set_smem(coalibi_fwd_kernel<64, true>, FwdLayout<64>::ALLOC);
-    ok &= set_smem(coalibi_decode_partial_kernel<128, false>, DecodeSmem<128>::BYTES);
-    ok &= set_smem(coalibi_decode_partial_kernel<128, true>, DecodeSmem<128>::BYTES);
-    ok &= set_smem(coalibi_decode_partial_kernel<64, false>, DecodeSmem<64>::BYTES);
-    ok &= set_smem(coalibi_decode_partial_kernel<64, true>, DecodeSmem<64>::BYTES);
+    ok &= set_smem(coalibi_decode_mma_kernel<128, false>, DecodeMmaSmem<128>::BYTES);
+    ok &= set_smem(coalibi_decode_mma_kernel<128, true>, DecodeMmaSmem<128>::BYTES);
+    ok &= set_smem(coalibi_decode_mma_kernel<64, false>, DecodeMmaSmem<64>::BYTES);
+    ok &= set_smem(coalibi_decode_mma_kernel<64, true>, DecodeMmaSmem<64>::BYTES);
     ok &= bwd_set_smem_attributes();
     st.status = ok ? COALIBI_OK : COALIBI_ERR_LAUNCH;
   });
@@ -261,8 +261,8 @@ namespace coalibi {
 namespace {
 template <int D, bool BF16>
 int launch_decode(const DecodeParams& p, cudaStream_t stream) {
-  const dim3 grid_p(p.B * p.Hkv, p.n_chunks, p.n_rgroups);
-  coalibi_decode_partial_kernel<D, BF16><<<grid_p, kDecodeBlock, DecodeSmem<D>::BYTES, stream>>>(p);
+  const dim3 grid_p(p.B * p.Hkv, p.n_chunks / 4, p.n_rgroups);
+  coalibi_decode_mma_kernel<D, BF16><<<grid_p, 128, DecodeMmaSmem<D>::BYTES, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) {
     coalibi_decode_combine_kernel<D, BF16><<<p.B * p.Hq * p.Sq, D, 0, stream>>>(p);
@@ -312,7 +312,7 @@ extern "C" int coalibi_fwd_decode(const CoalibiFwdArgs* a, void* workspace, size
   p.sm_scale = a->sm_scale;
   const DecodePlan pl = a->D == 128 ? decode_plan<128>(a->B, a->Hq, a->Hkv, a->Sq, a->Skv)
                                     : decode_plan<64>(a->B, a->Hq, a->Hkv, a->Sq, a->Skv);
-  p.n_chunks = pl.n_chunks;
+  p.n_chunks = pl.records;
   p.chunk_keys = pl.chunk_keys;
   p.n_rgroups = pl.n_rgroups;
   cudaStream_t s = static_cast<cudaStream_t>(stream);

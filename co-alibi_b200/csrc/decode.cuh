@@ -1,17 +1,17 @@
 // Co-ALiBi forward for few query rows against a long key/value sequence
-// ("decode": Sq <= 16, typically 1), on sm_100a CUDA cores.
+// ("decode": Sq <= 16, typically 1), on sm_100a.
 //
 // The forward kernel's 128-row query tiles would be almost empty here and the
 // work is a scan over K and V, so the path is HBM-bound and split over the keys:
 //
 //   partial kernel: one CTA per (batch, kv head, chunk of keys, group of up to 16
-//     query rows -- the G query heads of the kv head times the Sq rows).  It walks
-//     its chunk right to left in 128-key blocks staged in shared memory: scores
-//     (one thread per key, all rows), sigmoids, the inclusive sigmoid suffix sum
-//     restarted at 0 at the chunk's right end (warp shuffles plus a running carry
-//     across blocks), logits a' = c_a p - slope2 * z_local, an online softmax and
-//     O = sum 2^(a' - m) v (one thread per output dimension).  It writes the
-//     chunk's sigmoid total T, max m, sum l and unnormalised O.
+//     query rows -- the G query heads of the kv head times the Sq rows); each of
+//     its four warps takes a quarter of the chunk and walks it right to left in
+//     32-key steps: S = Q K^T and O += P V on the tensor cores (warp-level MMA,
+//     the 16 query rows padded), sigmoids, the inclusive sigmoid suffix sum
+//     restarted at 0 at the warp's right end, logits a' = c_a p - slope2 * z_local
+//     and an online softmax.  It writes the warp's sigmoid total T, max m, sum l
+//     and unnormalised O.
 //   combine kernel: one CTA per query row.  The keys right of chunk c add
 //     R_c = sum_{c' > c} T_c' to every z of chunk c, i.e. shift its logits by
 //     -slope2 * R_c: m'_c = m_c - slope2 * R_c, then the usual log-sum-exp merge
@@ -26,8 +26,8 @@
 namespace coalibi {
 
 constexpr int kDecodeMaxSq = 16;   // COALIBI_DECODE_MAX_SQ
-constexpr int kDecodeRows = 16;    // query rows per partial CTA
-constexpr int kDecodeBlock = 128;  // keys per shared-memory block (= threads per CTA)
+constexpr int kDecodeRows = 16;    // query rows per partial CTA (the MMA's M)
+constexpr int kDecodeBlock = 128;  // keys per CTA per step: four warps x 32
 
 struct DecodeParams {
   const void* q;
@@ -46,12 +46,15 @@ struct DecodeParams {
 };
 
 struct DecodePlan {
-  int n_chunks, chunk_keys, n_rgroups;
+  int cta_chunks;  // key chunks per (b, kv head, row group), one CTA each
+  int chunk_keys;  // keys per CTA chunk, a multiple of 128 (four warps x 32)
+  int n_rgroups;
+  int records;     // partial records per query row: four per CTA chunk (one per warp)
   size_t bytes;
 };
 
-// Chunking of the keys: about 1024 partial CTAs over (b, kv head, row group, chunk),
-// chunks a multiple of 128 keys, no empty chunk.
+// Chunking of the keys: about 512 CTAs over (b, kv head, row group, chunk), chunks
+// a multiple of 128 keys, no empty CTA chunk.
 template <int D>
 inline DecodePlan decode_plan(int B, int Hq, int Hkv, int Sq, int Skv) {
   DecodePlan pl;
@@ -59,12 +62,13 @@ inline DecodePlan decode_plan(int B, int Hq, int Hkv, int Sq, int Skv) {
   pl.n_rgroups = (G * Sq + kDecodeRows - 1) / kDecodeRows;
   const long long units = (long long)B * Hkv * pl.n_rgroups;
   const int blocks = (Skv + kDecodeBlock - 1) / kDecodeBlock;
-  int n = (int)((1024 + units - 1) / units);
+  int n = (int)((512 + units - 1) / units);
   n = n < 1 ? 1 : (n > blocks ? blocks : n);
   pl.chunk_keys = ((blocks + n - 1) / n) * kDecodeBlock;
-  pl.n_chunks = (Skv + pl.chunk_keys - 1) / pl.chunk_keys;
+  pl.cta_chunks = (Skv + pl.chunk_keys - 1) / pl.chunk_keys;
+  pl.records = 4 * pl.cta_chunks;
   const size_t rows = (size_t)B * Hq * Sq;
-  pl.bytes = rows * pl.n_chunks * (4 + D) * sizeof(float);
+  pl.bytes = rows * pl.records * (4 + D) * sizeof(float);
   return pl;
 }
 
@@ -76,260 +80,245 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc, boo
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all_but_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
+// Partial kernel.  Every warp of the CTA is its own chunk of the keys (a quarter
+// of the CTA's range, its own right-to-left suffix, merged by the combine kernel
+// like any other chunk), so no step inside a block needs the other warps.  Per 32-key step a warp stages K and V (cp.async, double-buffered,
+// padded rows), computes S = Q K^T with mma.m16n8k16 (Q: the 16 padded query
+// rows as A fragments held in registers), runs the sigmoid suffix scan on the C
+// fragments (quad shuffles within an 8-key tile, tile totals in registers),
+// exponentiates, and accumulates O += P V with P's C fragments reused as A
+// fragments and V read with ldmatrix.trans.
+// ---------------------------------------------------------------------------
+template <bool BF16>
+__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  if (BF16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
 
 template <int D>
-struct DecodeSmem {
-  static constexpr int KROW = D * 2 + 16;  // padded K rows: thread-per-key 16-byte reads hit distinct banks
-  static constexpr int KBUF = kDecodeBlock * KROW;
-  static constexpr int VBUF = kDecodeBlock * D * 2;
-  static constexpr int OFF_K = 0;                                          // [2] K blocks
-  static constexpr int OFF_V = OFF_K + 2 * KBUF;                           // [2] V blocks
-  static constexpr int OFF_Q = OFF_V + 2 * VBUF;                           // float [16][D]
-  static constexpr int OFF_E = OFF_Q + kDecodeRows * D * 4;                // float [128 keys][16 rows]
-  static constexpr int OFF_W = OFF_E + kDecodeBlock * kDecodeRows * 4;     // float [4 warps][16] sigmoid totals
-  static constexpr int OFF_X = OFF_W + 4 * kDecodeRows * 4;                // float [4 warps][16] block maxima
-  static constexpr int OFF_L = OFF_X + 4 * kDecodeRows * 4;                // float [4 warps][16] block row sums
-  static constexpr int OFF_R = OFF_L + 4 * kDecodeRows * 4;                // row state: m, carry, slope2, lim, l
-  static constexpr int BYTES = OFF_R + 5 * kDecodeRows * 4;
-  // PV: a thread owns two adjacent dimensions and one group of the block's keys
-  static constexpr int NGRP = kDecodeBlock / (D / 2);                    // key groups (2 for D=128, 4 for D=64)
-  static constexpr int KPG = kDecodeBlock / NGRP;                        // keys per group
-  static_assert((NGRP - 1) * kDecodeRows * D * 4 <= 2 * KBUF, "the group fold reuses the K buffers");
+struct DecodeMmaSmem {
+  static constexpr int STEP = 32;            // keys per warp step
+  static constexpr int ROW = D * 2 + 16;     // padded rows: the 8 rows of an ldmatrix hit distinct banks
+  static constexpr int TILE = STEP * ROW;    // one K or V step tile
+  static constexpr int PER_WARP = 4 * TILE;  // K and V, two buffers each
+  static constexpr int BYTES = 4 * PER_WARP;
 };
 
 template <int D, bool BF16>
-__global__ void __launch_bounds__(kDecodeBlock) coalibi_decode_partial_kernel(const DecodeParams p) {
-  using S = DecodeSmem<D>;
-  extern __shared__ __align__(16) uint8_t smem[];
-  float* qs = reinterpret_cast<float*>(smem + S::OFF_Q);
-  float* es = reinterpret_cast<float*>(smem + S::OFF_E);
-  float* wsum = reinterpret_cast<float*>(smem + S::OFF_W);
-  float* wmax = reinterpret_cast<float*>(smem + S::OFF_X);
-  float* wl = reinterpret_cast<float*>(smem + S::OFF_L);
-  float* m_s = reinterpret_cast<float*>(smem + S::OFF_R);
-  float* carry_s = m_s + kDecodeRows;
-  float* slope_s = carry_s + kDecodeRows;
-  int* lim_s = reinterpret_cast<int*>(slope_s + kDecodeRows);
-  float* l_s = reinterpret_cast<float*>(lim_s + kDecodeRows);
-
-  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const int bg = blockIdx.x;  // b * Hkv + g
-  const int c = blockIdx.y;   // key chunk (at most 1024 of them)
+__global__ void __launch_bounds__(128) coalibi_decode_mma_kernel(const DecodeParams p) {
+  using S = DecodeMmaSmem<D>;
+  constexpr int KK = D / 16;  // k-steps of QK^T, d-tile pairs of PV
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int gq = lane >> 2, tig = lane & 3;
+  const int bg = blockIdx.x, cc = blockIdx.y;
   const int b = bg / p.Hkv, g = bg - b * p.Hkv;
   const int G = p.Hq / p.Hkv;
-  const int r0 = blockIdx.z * kDecodeRows;
-  const int R = min(kDecodeRows, G * p.Sq - r0);
-  const int key_lo = c * p.chunk_keys;
-  const int key_hi = min(p.Skv, key_lo + p.chunk_keys);
+  const int r0 = blockIdx.z * 16;
+  const int R = min(16, G * p.Sq - r0);
+  const int sub = p.chunk_keys / 4;
+  const int lo = cc * p.chunk_keys + warp * sub;
+  const int hi = min(p.Skv, lo + sub);
   const float c_t = 0.5f * p.sm_scale;  // sigmoid(p) = 1/2 + tanh(p / 2) / 2
   const float c_a = p.sm_scale * kLog2e;
+  uint8_t* wbase = smem + warp * S::PER_WARP;
 
-  // local row u -> query head g*G + (r0+u)/Sq, query position (r0+u)%Sq
-  if (t < kDecodeRows) {
-    m_s[t] = -INFINITY;
-    carry_s[t] = 0.f;
-    l_s[t] = 0.f;
-    slope_s[t] = 0.f;
-    lim_s[t] = 0;
-    if (t < R) {
-      const int rr = r0 + t;
-      const int h = g * G + rr / p.Sq, i = rr % p.Sq;
-      slope_s[t] = load_slope(p.slopes, p.slopes_dtype, h) * kLog2e;
-      lim_s[t] = p.causal ? min(i + 1, p.Skv) : p.Skv;
+  // rows gq and gq + 8 of the 16 (padded) query rows
+  int lim[2];
+  float slope2[2];
+  bool rok[2];
+  size_t rowidx[2];
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    const int u = gq + 8 * x;
+    rok[x] = u < R;
+    const int rr = r0 + (rok[x] ? u : 0);
+    const int h = g * G + rr / p.Sq, i = rr % p.Sq;
+    lim[x] = rok[x] ? (p.causal ? min(i + 1, p.Skv) : p.Skv) : 0;
+    slope2[x] = load_slope(p.slopes, p.slopes_dtype, h) * kLog2e;
+    rowidx[x] = ((size_t)b * p.Hq + h) * p.Sq + i;
+  }
+  // Q as A fragments: a0 (row gq, cols 2tig..), a1 (row gq+8), a2 / a3 (cols + 8)
+  uint32_t qa[KK][4];
+  const uint16_t* qg = static_cast<const uint16_t*>(p.q);
+#pragma unroll
+  for (int kk = 0; kk < KK; ++kk) {
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        const size_t off = rowidx[x] * D + 16 * kk + 8 * hf + 2 * tig;
+        qa[kk][2 * hf + x] = rok[x] ? *reinterpret_cast<const uint32_t*>(qg + off) : 0u;
+      }
     }
   }
-  for (int idx = t; idx < kDecodeRows * D; idx += kDecodeBlock) {
-    const int u = idx / D, d = idx - u * D;
-    float x = 0.f;
-    if (u < R) {
-      const int rr = r0 + u;
-      const int h = g * G + rr / p.Sq, i = rr % p.Sq;
-      const uint16_t raw = static_cast<const uint16_t*>(p.q)[(((size_t)b * p.Hq + h) * p.Sq + i) * D + d];
-      x = BF16 ? __bfloat162float(__ushort_as_bfloat16(raw)) : __half2float(__ushort_as_half(raw));
-    }
-    qs[idx] = x;
-  }
-
-  // PV ownership: dimensions 2 * (t % (D/2)) and +1, keys of group t / (D/2)
-  const int dpair = t % (D / 2);
-  const int kgrp = t / (D / 2);
-  float2 oacc[kDecodeRows];
+  float o[2 * KK][4];
 #pragma unroll
-  for (int u = 0; u < kDecodeRows; ++u) oacc[u] = make_float2(0.f, 0.f);
+  for (int dn = 0; dn < 2 * KK; ++dn) o[dn][0] = o[dn][1] = o[dn][2] = o[dn][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_part[2] = {0.f, 0.f}, carry[2] = {0.f, 0.f};
 
-  constexpr int PIECES = D / 8;  // 16-byte pieces per row
-  const int nblk = (key_hi - key_lo + kDecodeBlock - 1) / kDecodeBlock;
-  // K (padded rows) and V of the 128 keys of block blk into buffer blk & 1, zeros past
-  // the chunk end; the copies run while the previous block is being processed
-  auto stage = [&](int blk) {
-    const int kb = key_lo + blk * kDecodeBlock;
-    uint8_t* kd = smem + S::OFF_K + (blk & 1) * S::KBUF;
-    uint8_t* vd = smem + S::OFF_V + (blk & 1) * S::VBUF;
+  const int nsteps = hi > lo ? (hi - lo + S::STEP - 1) / S::STEP : 0;
+  auto stage = [&](int st) {
+    const int kb = lo + st * S::STEP;
+    uint8_t* kt = wbase + (st & 1) * 2 * S::TILE;
+    uint8_t* vt = kt + S::TILE;
 #pragma unroll
-    for (int it = 0; it < PIECES; ++it) {
-      const int idx = it * kDecodeBlock + t;
-      const int j = idx / PIECES, pc = idx - j * PIECES;
-      const bool ok = kb + j < key_hi;
-      const size_t off = ok ? ((size_t)bg * p.Skv + kb + j) * D + pc * 8 : 0;
-      cp_async16(kd + j * S::KROW + pc * 16, static_cast<const uint16_t*>(p.k) + off, ok);
-      cp_async16(vd + (j * D + pc * 8) * 2, static_cast<const uint16_t*>(p.v) + off, ok);
+    for (int it = 0; it < D / 8; ++it) {
+      const int idx = it * 32 + lane;
+      const int key = idx / (D / 8), pc = idx - key * (D / 8);
+      const bool ok = kb + key < hi;
+      const size_t off = ok ? ((size_t)bg * p.Skv + kb + key) * D + pc * 8 : 0;
+      cp_async16(kt + key * S::ROW + pc * 16, static_cast<const uint16_t*>(p.k) + off, ok);
+      cp_async16(vt + key * S::ROW + pc * 16, static_cast<const uint16_t*>(p.v) + off, ok);
     }
   };
-  stage(nblk - 1);
+  if (nsteps > 0) stage(nsteps - 1);
   cp_async_commit();
-  for (int blk = nblk - 1; blk >= 0; --blk) {
-    const int kb = key_lo + blk * kDecodeBlock;
-    const uint8_t* ks = smem + S::OFF_K + (blk & 1) * S::KBUF;
-    const uint16_t* vs = reinterpret_cast<const uint16_t*>(smem + S::OFF_V + (blk & 1) * S::VBUF);
-    if (blk > 0) stage(blk - 1);
-    cp_async_commit();           // (an empty group on the last block keeps the count uniform)
-    cp_async_wait_all_but_one();  // this block's copies have landed
-    __syncthreads();              // ... for every thread; the row setup is visible too
-    // ---- scores q_u . k_key: thread t = key kb + t, all rows
-    const int key = kb + t;
-    float sc[kDecodeRows];
+  const int mat = lane >> 3, row8 = lane & 7;
+  for (int st = nsteps - 1; st >= 0; --st) {
+    if (st > 0) stage(st - 1);
+    cp_async_commit();
+    cp_async_wait_all_but_one();
+    __syncwarp();
+    const int kb = lo + st * S::STEP;
+    const uint32_t kt = smem_u32(wbase + (st & 1) * 2 * S::TILE);
+    const uint32_t vt = kt + S::TILE;
+    // ---- S = Q K^T: n-tile nt holds keys 8nt .. 8nt+7 of the step
+    float sc[4][4];
 #pragma unroll
-    for (int u = 0; u < kDecodeRows; ++u) sc[u] = 0.f;
-#pragma unroll 2
-    for (int pc = 0; pc < PIECES; ++pc) {
-      const uint4 kr = *reinterpret_cast<const uint4*>(ks + t * S::KROW + pc * 16);
-      const float2 k01 = unpack2<BF16>(kr.x), k23 = unpack2<BF16>(kr.y);
-      const float2 k45 = unpack2<BF16>(kr.z), k67 = unpack2<BF16>(kr.w);
+    for (int nt = 0; nt < 4; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
 #pragma unroll
-      for (int u = 0; u < kDecodeRows; ++u) {
-        if (u < R) {
-          const float4 qa = *reinterpret_cast<const float4*>(qs + u * D + pc * 8);
-          const float4 qb = *reinterpret_cast<const float4*>(qs + u * D + pc * 8 + 4);
-          float2 acc = __fmul2_rn(make_float2(qa.x, qa.y), k01);
-          acc = __ffma2_rn(make_float2(qa.z, qa.w), k23, acc);
-          acc = __ffma2_rn(make_float2(qb.x, qb.y), k45, acc);
-          acc = __ffma2_rn(make_float2(qb.z, qb.w), k67, acc);
-          sc[u] += acc.x + acc.y;
+    for (int kk = 0; kk < KK; ++kk) {
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        uint32_t b0, b1, b2, b3;
+        const int key = 16 * np + (mat >> 1) * 8 + row8;
+        ldsm_x4(kt + key * S::ROW + (16 * kk + (mat & 1) * 8) * 2, b0, b1, b2, b3);
+        mma16816<BF16>(sc[2 * np], qa[kk], b0, b1);
+        mma16816<BF16>(sc[2 * np + 1], qa[kk], b2, b3);
+      }
+    }
+    // ---- sigmoids, suffix sums (this warp's keys right of each key), logits, online max
+#pragma unroll
+    for (int x = 0; x < 2; ++x) {
+      float sg[4][2], excl[4], tt[4];
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = kb + 8 * nt + 2 * tig + e;
+          const bool vis = key < lim[x] && key < hi;
+          sg[nt][e] = vis ? fmaf(0.5f, tanh_approx(c_t * sc[nt][2 * x + e]), 0.5f) : 0.f;
+        }
+        const float pp = sg[nt][0] + sg[nt][1];
+        float inc = pp;  // inclusive suffix over the quad (keys grow with tig)
+        float y = __shfl_down_sync(0xffffffffu, inc, 1);
+        if (tig < 3) inc += y;
+        y = __shfl_down_sync(0xffffffffu, inc, 2);
+        if (tig < 2) inc += y;
+        tt[nt] = __shfl_sync(0xffffffffu, inc, lane & ~3);  // the tile's total
+        excl[nt] = inc - pp;
+      }
+      float right = carry[x], mx = -INFINITY;
+#pragma unroll
+      for (int nt = 3; nt >= 0; --nt) {
+        const float z1 = sg[nt][1] + excl[nt] + right;
+        const float z0 = z1 + sg[nt][0];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = kb + 8 * nt + 2 * tig + e;
+          const bool vis = key < lim[x] && key < hi;
+          const float a = vis ? fmaf(c_a, sc[nt][2 * x + e], -slope2[x] * (e ? z1 : z0)) : -INFINITY;
+          sc[nt][2 * x + e] = a;
+          mx = fmaxf(mx, a);
+        }
+        right += tt[nt];
+      }
+      carry[x] = right;
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(m_run[x], mx);
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      const float fac = (m_run[x] == -INFINITY) ? 0.f : ex2_approx(m_run[x] - m_use);
+      m_run[x] = m_new;
+      l_part[x] *= fac;
+#pragma unroll
+      for (int dn = 0; dn < 2 * KK; ++dn) {
+        o[dn][2 * x] *= fac;
+        o[dn][2 * x + 1] *= fac;
+      }
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float a = sc[nt][2 * x + e];
+          const float pe = (a == -INFINITY) ? 0.f : ex2_approx(a - m_use);
+          sc[nt][2 * x + e] = pe;
+          l_part[x] += pe;
         }
       }
     }
-    // ---- sigmoids and the inclusive suffix sum within each warp (keys grow with the lane)
-    float sf[kDecodeRows];
+    // ---- O += P V: P's C fragments of n-tiles 2kk2, 2kk2+1 form the A fragment of k-step kk2
 #pragma unroll
-    for (int u = 0; u < kDecodeRows; ++u) {
-      sf[u] = 0.f;
-      if (u < R) {
-        const bool vis = key < lim_s[u] && key < key_hi;
-        float x = vis ? fmaf(0.5f, tanh_approx(c_t * sc[u]), 0.5f) : 0.f;
+    for (int kk2 = 0; kk2 < 2; ++kk2) {
+      uint32_t pa[4];
+      pa[0] = pack2<BF16>(sc[2 * kk2][0], sc[2 * kk2][1]);
+      pa[1] = pack2<BF16>(sc[2 * kk2][2], sc[2 * kk2][3]);
+      pa[2] = pack2<BF16>(sc[2 * kk2 + 1][0], sc[2 * kk2 + 1][1]);
+      pa[3] = pack2<BF16>(sc[2 * kk2 + 1][2], sc[2 * kk2 + 1][3]);
 #pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-          const float y = __shfl_down_sync(0xffffffffu, x, off);
-          if (lane + off < 32) x += y;
-        }
-        if (lane == 0) wsum[warp * kDecodeRows + u] = x;
-        sf[u] = x;
+      for (int dp = 0; dp < KK; ++dp) {
+        uint32_t b0, b1, b2, b3;
+        const int key = 16 * kk2 + (mat & 1) * 8 + row8;
+        ldsm_x4_t(vt + key * S::ROW + (16 * dp + (mat >> 1) * 8) * 2, b0, b1, b2, b3);
+        mma16816<BF16>(o[2 * dp], pa, b0, b1);
+        mma16816<BF16>(o[2 * dp + 1], pa, b2, b3);
       }
     }
-    __syncthreads();
-    // ---- logits a' = c_a p - slope2 z, z = suffix within the chunk; block maxima
-#pragma unroll
-    for (int u = 0; u < kDecodeRows; ++u) {
-      if (u < R) {
-        const bool vis = key < lim_s[u] && key < key_hi;
-        float right = carry_s[u];
-        for (int w = warp + 1; w < kDecodeBlock / 32; ++w) right += wsum[w * kDecodeRows + u];
-        const float a = vis ? fmaf(c_a, sc[u], -slope_s[u] * (sf[u] + right)) : -INFINITY;
-        sc[u] = a;
-        float mx = a;
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-        if (lane == 0) wmax[warp * kDecodeRows + u] = mx;
-      }
-    }
-    __syncthreads();
-    // ---- exponentials against the running max; per-row rescale factor of O and l
-    float fac[kDecodeRows];
-#pragma unroll
-    for (int u = 0; u < kDecodeRows; ++u) {
-      fac[u] = 1.f;
-      if (u < R) {
-        float bm = wmax[u];
-#pragma unroll
-        for (int w = 1; w < kDecodeBlock / 32; ++w) bm = fmaxf(bm, wmax[w * kDecodeRows + u]);
-        const float m_old = m_s[u];
-        const float m_new = fmaxf(m_old, bm);
-        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-        const float e = (sc[u] == -INFINITY) ? 0.f : ex2_approx(sc[u] - m_use);
-        es[t * kDecodeRows + u] = e;
-        fac[u] = (m_old == -INFINITY) ? 0.f : ex2_approx(m_old - m_use);
-        float ls = e;  // the block's row sum
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
-        if (lane == 0) wl[warp * kDecodeRows + u] = ls;
-      }
-    }
-    __syncthreads();  // every thread has read m_s and written es
-    if (t < R) {
-      float bm = wmax[t], tot = 0.f, ls = 0.f;
-      for (int w = 0; w < kDecodeBlock / 32; ++w) {
-        bm = fmaxf(bm, wmax[w * kDecodeRows + t]);
-        tot += wsum[w * kDecodeRows + t];
-        ls += wl[w * kDecodeRows + t];
-      }
-      const float m_old = m_s[t];
-      const float m_use = (fmaxf(m_old, bm) == -INFINITY) ? 0.f : fmaxf(m_old, bm);
-      l_s[t] = fmaf(l_s[t], (m_old == -INFINITY) ? 0.f : ex2_approx(m_old - m_use), ls);
-      m_s[t] = fmaxf(m_old, bm);
-      carry_s[t] += tot;
-    }
-    // ---- O += sum_j e_j v_j over this thread's key group, two dimensions
-#pragma unroll
-    for (int u = 0; u < kDecodeRows; ++u) oacc[u] = __fmul2_rn(oacc[u], make_float2(fac[u], fac[u]));
-    const int j0 = kgrp * S::KPG;
-#pragma unroll 4
-    for (int jj = 0; jj < S::KPG; ++jj) {
-      const int j = j0 + jj;
-      const float2 vv = unpack2<BF16>(*reinterpret_cast<const uint32_t*>(vs + j * D + 2 * dpair));
-#pragma unroll
-      for (int u4 = 0; u4 < kDecodeRows / 4; ++u4) {
-        if (u4 * 4 < R) {
-          const float4 e = *reinterpret_cast<const float4*>(es + j * kDecodeRows + u4 * 4);
-          oacc[u4 * 4 + 0] = __ffma2_rn(make_float2(e.x, e.x), vv, oacc[u4 * 4 + 0]);
-          oacc[u4 * 4 + 1] = __ffma2_rn(make_float2(e.y, e.y), vv, oacc[u4 * 4 + 1]);
-          oacc[u4 * 4 + 2] = __ffma2_rn(make_float2(e.z, e.z), vv, oacc[u4 * 4 + 2]);
-          oacc[u4 * 4 + 3] = __ffma2_rn(make_float2(e.w, e.w), vv, oacc[u4 * 4 + 3]);
-        }
-      }
-    }
-    __syncthreads();  // every thread is done with this block's buffers before they are refilled
+    __syncwarp();  // this buffer is refilled by the prefetch two steps later
   }
-  // fold the key groups into group 0 (the K buffers are free now)
-  float* hx = reinterpret_cast<float*>(smem + S::OFF_K);
-  if (kgrp > 0) {
+  // ---- this warp's record: sigmoid total, max, sum and unnormalised O per row
+  const size_t rows = (size_t)p.B * p.Hq * p.Sq;
+  float* stats = p.ws;
+  float* obuf = p.ws + rows * p.n_chunks * 4;
 #pragma unroll
-    for (int u = 0; u < kDecodeRows; ++u)
-      if (u < R) *reinterpret_cast<float2*>(hx + ((kgrp - 1) * kDecodeRows + u) * D + 2 * dpair) = oacc[u];
-  }
-  __syncthreads();
-  if (kgrp == 0) {
-    for (int gi = 1; gi < S::NGRP; ++gi) {
+  for (int x = 0; x < 2; ++x) {
+    float l = l_part[x];
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    if (rok[x]) {
+      const size_t rec = rowidx[x] * p.n_chunks + cc * 4 + warp;
 #pragma unroll
-      for (int u = 0; u < kDecodeRows; ++u)
-        if (u < R) {
-          const float2 x = *reinterpret_cast<const float2*>(hx + ((gi - 1) * kDecodeRows + u) * D + 2 * dpair);
-          oacc[u] = __fadd2_rn(oacc[u], x);
-        }
-    }
-    const size_t rows = (size_t)p.B * p.Hq * p.Sq;
-    float* stats = p.ws;
-    float* obuf = p.ws + rows * p.n_chunks * 4;
-#pragma unroll
-    for (int u = 0; u < kDecodeRows; ++u) {
-      if (u < R) {
-        const int rr = r0 + u;
-        const int h = g * G + rr / p.Sq, i = rr % p.Sq;
-        const size_t row = ((size_t)b * p.Hq + h) * p.Sq + i;
-        const size_t rec = row * p.n_chunks + c;
-        *reinterpret_cast<float2*>(obuf + rec * D + 2 * dpair) = oacc[u];
-        if (dpair == 0) *reinterpret_cast<float4*>(stats + rec * 4) = make_float4(carry_s[u], m_s[u], l_s[u], 0.f);
-      }
+      for (int dn = 0; dn < 2 * KK; ++dn)
+        *reinterpret_cast<float2*>(obuf + rec * D + 8 * dn + 2 * tig) = make_float2(o[dn][2 * x], o[dn][2 * x + 1]);
+      if (tig == 0) *reinterpret_cast<float4*>(stats + rec * 4) = make_float4(carry[x], m_run[x], l, 0.f);
     }
   }
+  cp_async_wait_all();
 }
 
 // One CTA (D threads) per query row: merge the chunks right to left.

@@ -79,7 +79,7 @@ int coalibi_fwd(const CoalibiFwdArgs* args, void* stream);
  * against a long key/value sequence): the same arguments, mask semantics and
  * results (o, lse, rowsig) as coalibi_fwd, for the shapes the reference forward
  * launches with a nearly empty query block (co_alibi_attn/co_alibi_attn.py:44-57).
- * The keys are split into chunks reduced by separate CTAs on CUDA cores and merged
+ * The keys are split into chunks (one per warp of the partial kernel) and merged
  * exactly: the sigmoid totals of the chunks to the right shift each chunk's
  * logits.  workspace: device scratch of at least coalibi_fwd_decode_workspace_bytes()
  * bytes, 16-byte aligned; contents on entry do not matter.  Sq above the limit
