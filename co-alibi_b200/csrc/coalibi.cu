@@ -124,10 +124,12 @@ int device_setup(const void* ptr) {
     ok &= set_smem(coalibi_fwd_kernel<128, true>, FwdLayout<128>::ALLOC);
     ok &= set_smem(coalibi_fwd_kernel<64, false>, FwdLayout<64>::ALLOC);
     ok &= set_smem(coalibi_fwd_kernel<64, true>, FwdLayout<64>::ALLOC);
-    ok &= set_smem(coalibi_decode_mma_kernel<128, false>, DecodeMmaSmem<128>::BYTES);
-    ok &= set_smem(coalibi_decode_mma_kernel<128, true>, DecodeMmaSmem<128>::BYTES);
-    ok &= set_smem(coalibi_decode_mma_kernel<64, false>, DecodeMmaSmem<64>::BYTES);
-    ok &= set_smem(coalibi_decode_mma_kernel<64, true>, DecodeMmaSmem<64>::BYTES);
+    ok &= set_smem(coalibi_decode_mma_kernel<128, false, 32>, DecodeMmaSmem<128, 32>::BYTES);
+    ok &= set_smem(coalibi_decode_mma_kernel<128, true, 32>, DecodeMmaSmem<128, 32>::BYTES);
+    ok &= set_smem(coalibi_decode_mma_kernel<128, false, 16>, DecodeMmaSmem<128, 16>::BYTES);
+    ok &= set_smem(coalibi_decode_mma_kernel<128, true, 16>, DecodeMmaSmem<128, 16>::BYTES);
+    ok &= set_smem(coalibi_decode_mma_kernel<64, false, 16>, DecodeMmaSmem<64, 16>::BYTES);
+    ok &= set_smem(coalibi_decode_mma_kernel<64, true, 16>, DecodeMmaSmem<64, 16>::BYTES);
     ok &= bwd_set_smem_attributes();
     st.status = ok ? COALIBI_OK : COALIBI_ERR_LAUNCH;
   });
@@ -262,7 +264,15 @@ namespace {
 template <int D, bool BF16>
 int launch_decode(const DecodeParams& p, cudaStream_t stream) {
   const dim3 grid_p(p.B * p.Hkv, p.n_chunks / 4, p.n_rgroups);
-  coalibi_decode_mma_kernel<D, BF16><<<grid_p, 128, DecodeMmaSmem<D>::BYTES, stream>>>(p);
+  // 16-key warp steps halve the shared memory (three CTAs per SM instead of one at
+  // D = 128): faster at D = 64 and when several row groups re-read K and V from L2;
+  // one row group at D = 128 streams K and V at ~5 TB/s with 32-key steps
+  // (measured: B8 Hq32 Hkv8 Skv32768 0.213 vs 0.225 ms; Sq16 Skv131072 0.414 vs
+  // 0.322 ms; D64 B16 H12 Skv4096 0.052 vs 0.045 ms).
+  if (D == 64 || p.n_rgroups > 1)
+    coalibi_decode_mma_kernel<D, BF16, 16><<<grid_p, 128, DecodeMmaSmem<D, 16>::BYTES, stream>>>(p);
+  else
+    coalibi_decode_mma_kernel<D, BF16, 32><<<grid_p, 128, DecodeMmaSmem<D, 32>::BYTES, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) {
     coalibi_decode_combine_kernel<D, BF16><<<p.B * p.Hq * p.Sq, D, 0, stream>>>(p);

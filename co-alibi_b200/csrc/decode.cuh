@@ -7,7 +7,7 @@
 //   partial kernel: one CTA per (batch, kv head, chunk of keys, group of up to 16
 //     query rows -- the G query heads of the kv head times the Sq rows); each of
 //     its four warps takes a quarter of the chunk and walks it right to left in
-//     32-key steps: S = Q K^T and O += P V on the tensor cores (warp-level MMA,
+//     16- or 32-key steps: S = Q K^T and O += P V on the tensor cores (warp-level MMA,
 //     the 16 query rows padded), sigmoids, the inclusive sigmoid suffix sum
 //     restarted at 0 at the warp's right end, logits a' = c_a p - slope2 * z_local
 //     and an online softmax.  It writes the warp's sigmoid total T, max m, sum l
@@ -27,7 +27,7 @@ namespace coalibi {
 
 constexpr int kDecodeMaxSq = 16;   // COALIBI_DECODE_MAX_SQ
 constexpr int kDecodeRows = 16;    // query rows per partial CTA (the MMA's M)
-constexpr int kDecodeBlock = 128;  // keys per CTA per step: four warps x 32
+constexpr int kDecodeBlock = 128;  // CTA chunks are multiples of this many keys (four warps x 32)
 
 struct DecodeParams {
   const void* q;
@@ -85,7 +85,8 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 // ---------------------------------------------------------------------------
 // Partial kernel.  Every warp of the CTA is its own chunk of the keys (a quarter
 // of the CTA's range, its own right-to-left suffix, merged by the combine kernel
-// like any other chunk), so no step inside a block needs the other warps.  Per 32-key step a warp stages K and V (cp.async, double-buffered,
+// like any other chunk), so no step inside a block needs the other warps.  Per 16- or
+// 32-key step a warp stages K and V (cp.async, double-buffered,
 // padded rows), computes S = Q K^T with mma.m16n8k16 (Q: the 16 padded query
 // rows as A fragments held in registers), runs the sigmoid suffix scan on the C
 // fragments (quad shuffles within an 8-key tile, tile totals in registers),
@@ -119,18 +120,20 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
                : "r"(addr));
 }
 
-template <int D>
+template <int D, int STEP_ = 32>
 struct DecodeMmaSmem {
-  static constexpr int STEP = 32;            // keys per warp step
+  static constexpr int STEP = STEP_;         // keys per warp step (16 or 32)
+  static constexpr int NT = STEP / 8;        // 8-key n-tiles of S per step
   static constexpr int ROW = D * 2 + 16;     // padded rows: the 8 rows of an ldmatrix hit distinct banks
   static constexpr int TILE = STEP * ROW;    // one K or V step tile
   static constexpr int PER_WARP = 4 * TILE;  // K and V, two buffers each
   static constexpr int BYTES = 4 * PER_WARP;
 };
 
-template <int D, bool BF16>
+template <int D, bool BF16, int STEP = 32>
 __global__ void __launch_bounds__(128) coalibi_decode_mma_kernel(const DecodeParams p) {
-  using S = DecodeMmaSmem<D>;
+  using S = DecodeMmaSmem<D, STEP>;
+  constexpr int NT = S::NT;
   constexpr int KK = D / 16;  // k-steps of QK^T, d-tile pairs of PV
   extern __shared__ __align__(128) uint8_t smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -187,7 +190,7 @@ __global__ void __launch_bounds__(128) coalibi_decode_mma_kernel(const DecodePar
     uint8_t* kt = wbase + (st & 1) * 2 * S::TILE;
     uint8_t* vt = kt + S::TILE;
 #pragma unroll
-    for (int it = 0; it < D / 8; ++it) {
+    for (int it = 0; it < S::STEP * (D / 8) / 32; ++it) {
       const int idx = it * 32 + lane;
       const int key = idx / (D / 8), pc = idx - key * (D / 8);
       const bool ok = kb + key < hi;
@@ -208,13 +211,13 @@ __global__ void __launch_bounds__(128) coalibi_decode_mma_kernel(const DecodePar
     const uint32_t kt = smem_u32(wbase + (st & 1) * 2 * S::TILE);
     const uint32_t vt = kt + S::TILE;
     // ---- S = Q K^T: n-tile nt holds keys 8nt .. 8nt+7 of the step
-    float sc[4][4];
+    float sc[NT][4];
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+    for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < KK; ++kk) {
 #pragma unroll
-      for (int np = 0; np < 2; ++np) {
+      for (int np = 0; np < NT / 2; ++np) {
         uint32_t b0, b1, b2, b3;
         const int key = 16 * np + (mat >> 1) * 8 + row8;
         ldsm_x4(kt + key * S::ROW + (16 * kk + (mat & 1) * 8) * 2, b0, b1, b2, b3);
@@ -225,9 +228,9 @@ __global__ void __launch_bounds__(128) coalibi_decode_mma_kernel(const DecodePar
     // ---- sigmoids, suffix sums (this warp's keys right of each key), logits, online max
 #pragma unroll
     for (int x = 0; x < 2; ++x) {
-      float sg[4][2], excl[4], tt[4];
+      float sg[NT][2], excl[NT], tt[NT];
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
+      for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int key = kb + 8 * nt + 2 * tig + e;
@@ -245,7 +248,7 @@ __global__ void __launch_bounds__(128) coalibi_decode_mma_kernel(const DecodePar
       }
       float right = carry[x], mx = -INFINITY;
 #pragma unroll
-      for (int nt = 3; nt >= 0; --nt) {
+      for (int nt = NT - 1; nt >= 0; --nt) {
         const float z1 = sg[nt][1] + excl[nt] + right;
         const float z0 = z1 + sg[nt][0];
 #pragma unroll
@@ -272,7 +275,7 @@ __global__ void __launch_bounds__(128) coalibi_decode_mma_kernel(const DecodePar
         o[dn][2 * x + 1] *= fac;
       }
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
+      for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const float a = sc[nt][2 * x + e];
@@ -284,7 +287,7 @@ __global__ void __launch_bounds__(128) coalibi_decode_mma_kernel(const DecodePar
     }
     // ---- O += P V: P's C fragments of n-tiles 2kk2, 2kk2+1 form the A fragment of k-step kk2
 #pragma unroll
-    for (int kk2 = 0; kk2 < 2; ++kk2) {
+    for (int kk2 = 0; kk2 < NT / 2; ++kk2) {
       uint32_t pa[4];
       pa[0] = pack2<BF16>(sc[2 * kk2][0], sc[2 * kk2][1]);
       pa[1] = pack2<BF16>(sc[2 * kk2][2], sc[2 * kk2][3]);
