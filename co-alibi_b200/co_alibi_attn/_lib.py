@@ -39,7 +39,8 @@ class CoalibiBwdArgs(ctypes.Structure):
     ]
 
 
-EXPORTS = ("coalibi_fwd", "coalibi_fwd_decode", "coalibi_fwd_decode_workspace_bytes", "coalibi_bwd", "coalibi_bwd_phases", "coalibi_bwd_noalloc",
+EXPORTS = ("coalibi_fwd", "coalibi_fwd_decode", "coalibi_fwd_decode_workspace_bytes", "coalibi_bwd",
+           "coalibi_bwd_carry", "coalibi_bwd_phases", "coalibi_bwd_noalloc",
            "coalibi_bwd_workspace_bytes", "coalibi_selftest_wait_timeout", "coalibi_strerror",
            "coalibi_abi_version", "coalibi_last_error")
 
@@ -69,6 +70,8 @@ def load():
             lib.coalibi_fwd_decode_workspace_bytes.restype = c_size_t
             lib.coalibi_bwd.argtypes = [ctypes.POINTER(CoalibiBwdArgs), c_void_p]
             lib.coalibi_bwd.restype = c_int
+            lib.coalibi_bwd_carry.argtypes = [ctypes.POINTER(CoalibiBwdArgs), c_void_p, c_void_p]
+            lib.coalibi_bwd_carry.restype = c_int
             lib.coalibi_bwd_phases.argtypes = [ctypes.POINTER(CoalibiBwdArgs), c_int, c_void_p]
             lib.coalibi_bwd_phases.restype = c_int
             lib.coalibi_bwd_noalloc.argtypes = [ctypes.POINTER(CoalibiBwdArgs), c_void_p]

@@ -141,7 +141,11 @@ def _fwd(q, k, v, slopes, causal, sm_scale, decode=None):
     return o, lse, rowsig
 
 
-def _bwd(q, k, v, o, do, lse, rowsig, slopes, causal, sm_scale):
+def _bwd(q, k, v, o, do, lse, rowsig, slopes, causal, sm_scale, dA_carry_in=None):
+    """Backward kernels.  ``dA_carry_in`` (float32 [B, Hq, Sq]) marks k / v as one
+    key shard of longer rows (coalibi_bwd_carry): the sum of P (dP - delta) over the
+    keys left of the shard; o, lse and do are then the whole row's, rowsig the
+    sigmoid total of the shard and of every key right of it."""
     B, Hq, Sq, D = q.shape
     Hkv, Skv = k.shape[1], k.shape[2]
     lib = _lib.load()
@@ -160,7 +164,9 @@ def _bwd(q, k, v, o, do, lse, rowsig, slopes, causal, sm_scale):
         status=_status_word(q.device).data_ptr(), timeout_ms=0)
     stream = torch.cuda.current_stream(q.device).cuda_stream
     rec = kernel_events
-    if rec is None:
+    if dA_carry_in is not None:
+        _lib.check(lib.coalibi_bwd_carry(a, dA_carry_in.data_ptr(), stream), "coalibi_bwd_carry")
+    elif rec is None:
         _lib.check(lib.coalibi_bwd(a, stream), "coalibi_bwd")
     else:
         for bit, name in ((1, "bwd_delta"), (2, "bwd_a"), (4, "bwd_b")):

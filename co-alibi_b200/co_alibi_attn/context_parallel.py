@@ -1,0 +1,230 @@
+"""Sequence (context) parallel Co-ALiBi: rows whose keys are split into shards.
+
+The reference has no sequence parallelism (its backward keeps O(S^2) partials,
+``co_alibi_attn/co_alibi_attn.py:91-96``); this module evaluates attention over
+key shards with the sm_100a kernels and merges the pieces exactly.
+
+Forward.  For a query row and key shard c, the kernels compute the shard's
+output o_c, log-sum-exp lse_c and sigmoid total T_c with the sigmoid suffix sum z
+restarted at the shard's right end.  The keys right of shard c add
+R_c = sum_{c' > c} T_c' to every z in it, i.e. shift its logits by -slope * R_c,
+so lse'_c = lse_c - slope * R_c, and the whole row is the log-sum-exp merge:
+LSE = logsumexp_c lse'_c, O = sum_c exp(lse'_c - LSE) o_c, rowsig = sum_c T_c.
+
+Backward.  Per key shard the backward kernels take the whole row's O, LSE and dO,
+rowsig = T_c + R_c (so z is the global suffix) and the dA prefix carried in from
+the shards to the left, C_c = sum_{c' < c} w_c' (dO . o_c' - delta) with
+w_c = exp(lse'_c - LSE) and delta = dO . O (coalibi_bwd_carry); dq sums over the
+shards, dk / dv of a shard over the query shards that see it.
+
+With causal masking the query and key shards share boundaries: query shard r sees
+key shards c < r unmasked and shard r with the top-left mask.
+
+``sequence_sharded_attention`` runs the shards one after another on one device
+(the building block, and its check); ``ring_attention`` gives every rank of a
+process group one sequence shard of q, k, v and passes key / value shards (and,
+in the backward, dk / dv accumulators) around the ring.
+"""
+import torch
+import torch.distributed as dist
+
+from .co_alibi_attn import _api_slopes, _bwd, _check_inputs, _fwd
+
+__all__ = ["sequence_sharded_attention", "ring_attention"]
+
+
+def _kernel_fwd(q, k, v, slopes, causal, sm_scale):
+    return _fwd(q.contiguous(), k.contiguous(), v.contiguous(), slopes, causal, sm_scale)
+
+
+def _kernel_bwd(q, k, v, o, do, lse, rowsig, slopes, causal, sm_scale, carry_in):
+    return _bwd(q.contiguous(), k.contiguous(), v.contiguous(), o, do, lse.contiguous(), rowsig.contiguous(),
+                slopes, causal, sm_scale, dA_carry_in=carry_in.contiguous())
+
+
+def _f(x):
+    """float32 for the merge arithmetic (float64 kept, for float64 stand-ins)."""
+    return x if x.dtype == torch.float64 else x.float()
+
+
+class _RowMerge:
+    """Right-to-left merge of one query shard's key-shard partials."""
+
+    def __init__(self, slopes):
+        self.sl = _f(slopes).view(1, -1, 1)
+        self.parts = {}  # c -> (o_c, lse_c, T_c)
+
+    def add(self, c, o_c, lse_c, t_c):
+        self.parts[c] = (o_c, _f(lse_c), _f(t_c))
+
+    def finish(self, dtype):
+        """Merged (O, LSE, rowsig) and, per shard, (o_c, shifted lse'_c, T_c, R_c)."""
+        R = None
+        lse_all = o_all = None
+        self.shifted = {}
+        for c in sorted(self.parts, reverse=True):  # right to left
+            o_c, lse_c, t_c = self.parts[c]
+            if R is None:
+                R = torch.zeros_like(t_c)
+            lse_p = lse_c - self.sl.to(lse_c.dtype) * R
+            self.shifted[c] = (o_c, lse_p, t_c, R)
+            if lse_all is None:
+                lse_all, o_all = lse_p, _f(o_c)
+            else:
+                new = torch.logaddexp(lse_all, lse_p)
+                o_all = o_all * torch.exp(lse_all - new).unsqueeze(-1) + _f(o_c) * torch.exp(lse_p - new).unsqueeze(-1)
+                lse_all = new
+            R = R + t_c
+        self.lse, self.rowsig = lse_all, R
+        return o_all.to(dtype), lse_all, R
+
+    def carries(self, o, do):
+        """dA carry-in C_c of every shard (left to right) for the row's O and dO."""
+        delta = (_f(do) * _f(o)).sum(-1)
+        C, out = torch.zeros_like(delta), {}
+        for c in sorted(self.shifted):
+            o_c, lse_p, t_c, R = self.shifted[c]
+            out[c] = C
+            w = torch.exp(lse_p - self.lse)
+            C = C + w * ((_f(do) * _f(o_c)).sum(-1) - delta)
+        return out
+
+
+def _split(x, n):
+    S = x.shape[2]
+    step = -(-S // n)
+    return [x[:, :, i:i + step] for i in range(0, S, step)]
+
+
+class _SequenceSharded(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, slopes, n_shards, causal, sm_scale, fwd_fn, bwd_fn):
+        qs, ks, vs = _split(q, n_shards), _split(k, n_shards), _split(v, n_shards)
+        if causal and [t.shape[2] for t in qs] != [t.shape[2] for t in ks]:
+            raise ValueError("causal sequence sharding needs Sq == Skv (shared shard boundaries)")
+        outs, merges = [], []
+        for r, q_r in enumerate(qs):
+            m = _RowMerge(slopes)
+            for c in range(len(ks)):
+                if causal and c > r:
+                    continue
+                m.add(c, *fwd_fn(q_r, ks[c], vs[c], slopes, causal and c == r, sm_scale))
+            o_r, _, _ = m.finish(q.dtype)
+            outs.append(o_r)
+            merges.append(m)
+        o = torch.cat(outs, dim=2)
+        ctx.save_for_backward(q, k, v, o, slopes)
+        ctx.merges, ctx.n_shards, ctx.causal, ctx.sm_scale = merges, n_shards, causal, sm_scale
+        ctx.bwd_fn = bwd_fn
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, slopes = ctx.saved_tensors
+        n, causal, scale = ctx.n_shards, ctx.causal, ctx.sm_scale
+        qs, ks, vs = _split(q, n), _split(k, n), _split(v, n)
+        os_, dos = _split(o, n), _split(do.to(q.dtype).contiguous(), n)
+        acc = torch.promote_types(q.dtype, torch.float32)
+        dq = [torch.zeros(t.shape, dtype=acc, device=q.device) for t in qs]
+        dk = [torch.zeros(t.shape, dtype=acc, device=q.device) for t in ks]
+        dv = [torch.zeros(t.shape, dtype=acc, device=q.device) for t in vs]
+        for r, m in enumerate(ctx.merges):
+            o_r, do_r = os_[r].contiguous(), dos[r].contiguous()
+            carry = m.carries(o_r, do_r)
+            for c, (o_c, lse_p, t_c, R) in m.shifted.items():
+                g = ctx.bwd_fn(qs[r], ks[c], vs[c], o_r, do_r, m.lse, t_c + R, slopes, causal and c == r, scale,
+                               carry[c])
+                dq[r] += g[0].to(acc)
+                dk[c] += g[1].to(acc)
+                dv[c] += g[2].to(acc)
+        cat = lambda xs, t: torch.cat(xs, dim=2).to(t.dtype)  # noqa: E731
+        return cat(dq, q), cat(dk, k), cat(dv, v), None, None, None, None, None, None
+
+
+def sequence_sharded_attention(q, k, v, n_shards, causal=True, sm_scale=None, bias_max=8.0, _shard_fns=None):
+    """``co_alibi_attention`` evaluated over ``n_shards`` sequence shards on one
+    device and merged exactly (forward and backward); the single-device form of
+    ``ring_attention``.  ``_shard_fns`` as in ``ring_attention``."""
+    if sm_scale is None:
+        sm_scale = 1.0 / (q.shape[-1] ** 0.5)
+    fwd_fn, bwd_fn = _shard_fns or (_kernel_fwd, _kernel_bwd)
+    slopes = _api_slopes(q.shape[1], bias_max, q.dtype, q.device)
+    if _shard_fns is None:
+        _check_inputs(q, k, v, slopes)
+    return _SequenceSharded.apply(q.contiguous(), k.contiguous(), v.contiguous(), slopes, n_shards, causal, sm_scale,
+                                  fwd_fn, bwd_fn)
+
+
+# ---------------------------------------------------------------------------
+# ring over a process group: rank r holds sequence shard r of q, k, v
+# ---------------------------------------------------------------------------
+def _ring_pass(tensors, group):
+    """Send ``tensors`` to the next rank, return the previous rank's."""
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    nxt = dist.get_global_rank(group, (rank + 1) % world) if group is not None else (rank + 1) % world
+    prv = dist.get_global_rank(group, (rank - 1) % world) if group is not None else (rank - 1) % world
+    recv = [torch.empty_like(t) for t in tensors]
+    ops = [dist.P2POp(dist.isend, t, nxt, group) for t in tensors] + \
+          [dist.P2POp(dist.irecv, t, prv, group) for t in recv]
+    for req in dist.batch_isend_irecv(ops):
+        req.wait()
+    return recv
+
+
+class _Ring(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, slopes, causal, sm_scale, group, fwd_fn, bwd_fn):
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        m = _RowMerge(slopes)
+        kv = [k, v]
+        for s in range(world):
+            c = (rank - s) % world
+            if not (causal and c > rank):
+                m.add(c, *fwd_fn(q, kv[0], kv[1], slopes, causal and c == rank, sm_scale))
+            if s + 1 < world:
+                kv = _ring_pass(kv, group)
+        o, _, _ = m.finish(q.dtype)
+        ctx.save_for_backward(q, k, v, o, slopes)
+        ctx.m, ctx.causal, ctx.sm_scale, ctx.group, ctx.bwd_fn = m, causal, sm_scale, group, bwd_fn
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, slopes = ctx.saved_tensors
+        group, m, causal, scale = ctx.group, ctx.m, ctx.causal, ctx.sm_scale
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        do = do.to(q.dtype).contiguous()
+        carry = m.carries(o, do)
+        acc = torch.promote_types(q.dtype, torch.float32)
+        dq = torch.zeros(q.shape, dtype=acc, device=q.device)
+        # key / value shard c travels with the float32 dk / dv accumulators of shard c
+        buf = [k, v, torch.zeros(k.shape, dtype=acc, device=k.device), torch.zeros(v.shape, dtype=acc, device=v.device)]
+        for s in range(world):
+            c = (rank - s) % world
+            if c in m.shifted:
+                o_c, lse_p, t_c, R = m.shifted[c]
+                g = ctx.bwd_fn(q, buf[0], buf[1], o, do, m.lse, t_c + R, slopes, causal and c == rank, scale,
+                               carry[c])
+                dq += g[0].to(acc)
+                buf[2] += g[1].to(acc)
+                buf[3] += g[2].to(acc)
+            buf = _ring_pass(buf, group) if s + 1 < world else _ring_pass(buf[2:], group)
+        # after `world` passes the accumulators of shard `rank` are back here
+        return dq.to(q.dtype), buf[0].to(k.dtype), buf[1].to(v.dtype), None, None, None, None, None, None
+
+
+def ring_attention(q, k, v, causal=True, sm_scale=None, bias_max=8.0, group=None, _shard_fns=None):
+    """Co-ALiBi attention over a sequence split across the ranks of ``group``:
+    rank r passes its contiguous shard r of q [B, Hq, S_r, D] and k, v
+    [B, Hkv, S_r, D] (all heads; equal shard lengths) and gets its rows of the
+    output, with gradients for its shards.  Key / value shards travel around the
+    ring; no rank holds the whole sequence.  ``_shard_fns`` (tests only) replaces
+    the per-shard kernels with a (forward, backward) pair of the same signature."""
+    if sm_scale is None:
+        sm_scale = 1.0 / (q.shape[-1] ** 0.5)
+    fwd_fn, bwd_fn = _shard_fns or (_kernel_fwd, _kernel_bwd)
+    slopes = _api_slopes(q.shape[1], bias_max, q.dtype, q.device)
+    if _shard_fns is None:
+        _check_inputs(q, k, v, slopes)
+    return _Ring.apply(q.contiguous(), k.contiguous(), v.contiguous(), slopes, causal, sm_scale, group, fwd_fn,
+                       bwd_fn)

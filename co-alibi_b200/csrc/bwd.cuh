@@ -75,6 +75,9 @@ struct BwdParams {
   int n_kb32;     // ceil(Skv / 32): carry entries per row
   int n_blocks;   // pass-B key blocks: ceil(Skv / KB)
   int sq_pad;
+  // optional [B * Hq * Sq]: dA prefix carried in from keys left of this call's keys
+  // (the call is one key shard of a longer row); null = 0
+  const float* c_init;
 };
 
 // ---------------------------------------------------------------------------
@@ -534,8 +537,9 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
                          : bwd_a_da<false>(xa + 16 * hh, sg + 16 * hh, dpr, key0 + 16 * hh, lim, slope2, delta, zz);
         }
       }
-      // dA prefix sum before this chunk's first key, handed along the same way
-      float cc = 0.f;
+      // dA prefix sum before this chunk's first key, handed along the same way (the
+      // first chunk of the row starts from the carry-in, 0 unless a key shard)
+      float cc = (p.c_init != nullptr && row_ok && wg == 0 && n == 0) ? p.c_init[ri] : 0.f;
       if (ok && (wg > 0 || n > 0)) {
         ok = mbar_wait(&clink[quarter * L::NWG + wg], (wg > 0 ? n : n - 1) & 1, g);
         cc = xd[wg * 128 + t_row];
@@ -1502,8 +1506,9 @@ inline bool bwd_set_smem_attributes() {
 
 template <int D, bool BF16>
 inline int bwd_launch_t(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigned long long tmo,
-                        cudaStream_t stream, int phases) {
+                        cudaStream_t stream, int phases, const float* c_init) {
   BwdParams p{};
+  p.c_init = c_init;
   p.o = a.o;
   p.dout = a.dout;
   p.lse = a.lse;
@@ -1560,13 +1565,13 @@ inline int bwd_launch_t(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigne
 }
 
 inline int bwd_launch(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigned long long tmo,
-                      cudaStream_t stream, int phases) {
+                      cudaStream_t stream, int phases, const float* c_init = nullptr) {
   const bool bf16 = a.dtype == COALIBI_BF16;
   if (a.D == 128)
-    return bf16 ? bwd_launch_t<128, true>(a, ws, tmo, stream, phases)
-                : bwd_launch_t<128, false>(a, ws, tmo, stream, phases);
-  return bf16 ? bwd_launch_t<64, true>(a, ws, tmo, stream, phases)
-              : bwd_launch_t<64, false>(a, ws, tmo, stream, phases);
+    return bf16 ? bwd_launch_t<128, true>(a, ws, tmo, stream, phases, c_init)
+                : bwd_launch_t<128, false>(a, ws, tmo, stream, phases, c_init);
+  return bf16 ? bwd_launch_t<64, true>(a, ws, tmo, stream, phases, c_init)
+              : bwd_launch_t<64, false>(a, ws, tmo, stream, phases, c_init);
 }
 
 }  // namespace coalibi

@@ -358,6 +358,23 @@ extern "C" int coalibi_bwd_phases(const CoalibiBwdArgs* a, int phase_mask, void*
 
 extern "C" int coalibi_bwd(const CoalibiBwdArgs* a, void* stream) { return coalibi_bwd_phases(a, 7, stream); }
 
+extern "C" int coalibi_bwd_carry(const CoalibiBwdArgs* a, const float* dA_carry_in, void* stream) {
+  if (a == nullptr || dA_carry_in == nullptr) return COALIBI_ERR_NULL_POINTER;
+  if (!a->q || !a->k || !a->v || !a->o || !a->dout || !a->lse || !a->rowsig || !a->slopes || !a->dq || !a->dk ||
+      !a->dv)
+    return COALIBI_ERR_NULL_POINTER;
+  int rc = check_common(a->B, a->Hq, a->Hkv, a->Sq, a->Skv, a->D, a->dtype, a->slopes_dtype);
+  if (rc) return rc;
+  const void* ptrs[8] = {a->q, a->k, a->v, a->o, a->dout, a->dq, a->dk, a->dv};
+  for (const void* ptr : ptrs)
+    if (!aligned16(ptr)) return COALIBI_ERR_ALIGNMENT;
+  const BwdWorkspace ws = bwd_workspace_layout(a->B, a->Hq, a->Sq, a->Skv);
+  if (a->workspace == nullptr || a->workspace_bytes < ws.total) return COALIBI_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0) return COALIBI_ERR_ALIGNMENT;
+  if ((rc = device_setup(a->q))) return rc;
+  return bwd_launch(*a, ws, timeout_ns(a->timeout_ms), static_cast<cudaStream_t>(stream), 7, dA_carry_in);
+}
+
 extern "C" const char* coalibi_strerror(int code) {
   switch (code) {
     case COALIBI_OK: return "ok";

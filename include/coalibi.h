@@ -121,6 +121,15 @@ size_t coalibi_bwd_workspace_bytes(int B, int Hq, int Hkv, int Sq, int Skv, int 
 
 int coalibi_bwd(const CoalibiBwdArgs* args, void* stream);
 
+/* Backward of one key shard of longer rows (sequence / context parallelism, which
+ * the reference does not have): the keys of this call are a contiguous piece of
+ * each row's keys.  Same arguments as coalibi_bwd, read this way: o, lse and dout
+ * are those of the whole row (so delta and P are global); rowsig is the sigmoid
+ * total of this call's keys plus that of every key right of them; dA_carry_in
+ * [B * Hq * Sq] float32 is sum_t P_it (dP_it - delta_i) over the keys left of them.
+ * dq, dk and dv are this shard pair's contributions (sum them over the shards). */
+int coalibi_bwd_carry(const CoalibiBwdArgs* args, const float* dA_carry_in, void* stream);
+
 /* Profiling aid with no counterpart in the reference: launch only the backward
  * kernels selected by phase_mask (bit 0: delta = rowsum(dO * O) pre-pass, bit 1:
  * pass A -> dq and the per-32-key carries in the workspace, bit 2: pass B -> dk, dv).

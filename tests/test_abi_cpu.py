@@ -70,6 +70,8 @@ def test_bwd_validation_and_phase_mask():
     assert lib.coalibi_bwd_phases(ctypes.byref(a), 8, None) == 4  # bad phase mask
     a.workspace, a.workspace_bytes = 256 + 16, 1 << 20
     assert lib.coalibi_bwd(ctypes.byref(a), None) == 5          # workspace not 256-aligned
+    assert lib.coalibi_bwd_carry(ctypes.byref(a), None, None) == 1  # no dA carry
+    assert lib.coalibi_bwd_carry(ctypes.byref(a), 16, None) == 5    # (then the same checks as coalibi_bwd)
     big = _lib.CoalibiBwdArgs(**{f: getattr(a, f) for f, _ in _lib.CoalibiBwdArgs._fields_})
     big.B, big.Hq, big.Hkv, big.Sq, big.Skv, big.D = 8, 16, 16, 4096, 4096, 128
     assert lib.coalibi_bwd_noalloc(ctypes.byref(big), None) == 8  # exceeds the static scratch
