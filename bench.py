@@ -1,7 +1,7 @@
 """Benchmark of the Co-ALiBi hot path (forward + backward) on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config cfg2|cfg3|cfg4|cfg5] [--scaling weak|strong]
+                    [--config cfg2|cfg3|cfg4|cfg5|decode|cp] [--scaling weak|strong]
 
 One step = co_alibi_attention(q, k, v, causal) forward and backward over one
 batch of the named configuration (default cfg2: B=8, H=16, S=4096, D=128, fp16,
@@ -17,6 +17,9 @@ and the maximum over ranks is reported.
 ``--config cfg5`` instead times one data-parallel training step of the small
 Co-ALiBi GPT (co_alibi_gpt: 12 layers, d_model 768, 12 heads of D=64, seq 1024,
 batch 32 per GPU, bf16, DDP over NCCL, AdamW) and reports tokens per second.
+``--config decode`` times one new query row against a 32,768-key cache;
+``--config cp`` one 65,536-token causal sequence split over the N GPUs
+(context parallelism, ring over NCCL).
 
 Prints ONE JSON line (rank 0).  ``--impl reference`` times the reference
 algorithm's CPU path (the oracle restatement of model.py, on all host cores)
@@ -412,6 +415,139 @@ def run_decode(args, world, rank, local_rank, dev):
         print(json.dumps(line), flush=True)
 
 
+CP_SHAPE = (1, 32, 8, 65536, 128)   # B, Hq, Hkv, S, D of the context-parallel line
+
+
+def run_cp(args, world, rank, local_rank, dev):
+    """cp: one long causal sequence (B=1, Hq=32, Hkv=8, S=65,536, D=128, bf16)
+    forward + backward through context_parallel.ring_attention with the zig-zag
+    layout: the sequence in 2N chunks, rank r holding chunks r and 2N-1-r, key /
+    value chunks (and dk / dv accumulators) passed around the NCCL ring.  Total
+    work is fixed ("strong"); value = the whole sequence's algorithmic FLOPs per
+    second."""
+    import torch.distributed as dist
+    import co_alibi_attn
+    import co_alibi_attn.co_alibi_attn as impl
+    from co_alibi_attn.context_parallel import chunk_layout, ring_attention
+    B, Hq, Hkv, S, D = CP_SHAPE
+    dt = torch.bfloat16
+    own = chunk_layout("zigzag", world, rank)
+    L = S // (2 * world)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def chunk(i):
+        g = torch.Generator().manual_seed(3000 + i)
+        return (torch.randn(B, Hq, L, D, generator=g).to(dt), torch.randn(B, Hkv, L, D, generator=g).to(dt),
+                torch.randn(B, Hkv, L, D, generator=g).to(dt), torch.randn(B, Hq, L, D, generator=g).to(dt))
+
+    parts = [chunk(i) for i in own]
+    hosts = [torch.cat([p[j] for p in parts], dim=2).pin_memory() for j in range(4)]
+    q, k, v, do = (h.to(dev) for h in hosts)
+    for t in (q, k, v):
+        t.requires_grad_(True)
+
+    def step():
+        o = ring_attention(q, k, v, causal=True, layout="zigzag")
+        o.backward(do)
+        q.grad = k.grad = v.grad = None
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    assert co_alibi_attn.device_status(reset=True) == 0, "kernel-side error during warmup"
+    impl.kernel_events = {}
+    sampler = ClockSampler(physical_gpu_index(local_rank))
+    sampler.start()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    rec = impl.kernel_events
+    impl.kernel_events = None
+    status = co_alibi_attn.device_status(reset=True)
+    ms = e0.elapsed_time(e1) / args.steps
+    kern = {name: sum(a.elapsed_time(b) for a, b in pairs) / args.steps for name, pairs in rec.items()}
+    launches = {name: len(pairs) // args.steps for name, pairs in rec.items()}
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = t.item()
+    E_all = visible(S, True) * B * Hq
+    flops_step = 14.0 * D * E_all
+    value = flops_step / (ms_max * 1e-3) / 1e12
+    # this rank's visible scores: pairs (i, j <= i) of its chunks against all chunks
+    E_rank = sum((i * L * L + L * (L + 1) // 2) for i in own) * B * Hq
+    kern_ms = kern.get("fwd", 0.0) + kern.get("bwd_carry", 0.0)
+    ach = 14.0 * D * E_rank / (kern_ms * 1e-3) / 1e12
+    # e2e: this rank's chunks from pinned host memory, o / dq / dk / dv back, every step
+    outs = [torch.empty_like(hosts[0]).pin_memory(), torch.empty_like(hosts[0]).pin_memory(),
+            torch.empty_like(hosts[1]).pin_memory(), torch.empty_like(hosts[2]).pin_memory()]
+    qd, kd, vd, dod = (torch.empty_like(x) for x in (q, k, v, do))
+
+    def e2e_step():
+        for dst, src in zip((qd, kd, vd, dod), hosts):
+            dst.copy_(src, non_blocking=True)
+        qi, ki, vi = (x.detach().requires_grad_(True) for x in (qd, kd, vd))
+        o = ring_attention(qi, ki, vi, causal=True, layout="zigzag")
+        o.backward(dod)
+        for dst, src in zip(outs, (o, qi.grad, ki.grad, vi.grad)):
+            dst.copy_(src, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_e2e = max(1, args.e2e_steps)
+    f0.record()
+    for _ in range(n_e2e):
+        e2e_step()
+    f1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([f0.elapsed_time(f1) / n_e2e], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = t.item()
+    burst, sustained, hbm, peak_src = load_peaks()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tfl, tsec, nth, desc = cpu_sample_tflops((B, Hq, Hkv, S, D, dt, True, 1.0, False), 256, 3)
+        cpu = {"value": round(tfl, 6), "unit": "TFLOP/s", "cores": nth, "kind": "port", "sample": desc,
+               "seconds_per_sample": round(tsec, 3)}
+    if rank == 0:
+        line = {
+            "metric": metric_name("cp"), "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"cp: ring_attention fwd+bwd (context parallel, zig-zag chunks), B={B} Hq={Hq} "
+                                   f"Hkv={Hkv} S={S} D={D} bf16 causal", "global_batch": B, "seq_len": S,
+                       "parallelism": f"sequence x{world} ({2 * world} zig-zag chunks, NCCL ring)",
+                       "l2": "q, do (512 MiB each at N=1) exceed the 126 MB L2; no flush needed"},
+            "roofline": {"bound": "tensor", "kernel": "fwd + bwd_carry pair kernels (rank 0)", "achieved": round(ach, 2),
+                         "peak": sustained, "unit": "TFLOP/s", "frac": round(ach / sustained, 4),
+                         "peak_source": f"{peak_src} bf16_tflops_sustained", "traffic": None,
+                         "kernel_ms": round(kern_ms, 3), "merge_and_ring_ms": round(ms - kern_ms, 3),
+                         "note": "rank 0's algorithmic FLOPs (14 D per visible score) / the summed CUDA-event time "
+                                 "of its pair kernels; the rest of the step is the merge arithmetic, the carries and "
+                                 "the ring transfers not hidden behind the kernels"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(flops_step / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+                    "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": sum(h.numel() * 2 for h in hosts),
+                    "d2h_bytes_per_step": sum(x.numel() * 2 for x in outs)},
+            "gpu_launches": launches.get("fwd", 0) + 3 * launches.get("bwd_carry", 0),
+            "clocks": clocks, "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+
+
 def gpt_cpu_sample(cfg):
     """The same GPT, float32 on the host cores, the attention from the oracle
     (the reference's own maths restated): one sequence forward + backward."""
@@ -440,7 +576,8 @@ def metric_name(config):
             "cfg3": "fwd+bwd TFLOP/s (algorithmic causal), GQA B4 Hq32 Hkv8 S8192 D128 bf16 causal",
             "cfg4": "fwd TFLOP/s, B16 H12 S2048 D64 fp16 non-causal",
             "cfg5": "Co-ALiBi GPT training step tokens/s (12 layers, d768, 12 heads D64, seq 1024, batch 32 per GPU)",
-            "decode": "decode query rows/s, B8 Hq32 Hkv8 Sq1 Skv32768 D128 bf16"}[config]
+            "decode": "decode query rows/s, B8 Hq32 Hkv8 Sq1 Skv32768 D128 bf16",
+            "cp": "context-parallel fwd+bwd TFLOP/s (algorithmic causal), B1 Hq32 Hkv8 S65536 D128 bf16"}[config]
 
 
 def config_dict(args, cfg):
@@ -464,7 +601,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS) + ["cfg5", "decode"])
+    ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS) + ["cfg5", "decode", "cp"])
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--batch", type=int, default=None,
@@ -472,11 +609,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    if args.config in ("cfg5", "decode"):
+    if args.config in ("cfg5", "decode", "cp"):
         if args.impl == "reference":
             if int(os.environ.get("RANK", "0")) == 0:
-                why = ("the reference ships no model code; cfg5 is a caller built here" if args.config == "cfg5" else
-                       "the decode line is an addition of this build; the reference arm is the default config's")
+                why = {"cfg5": "the reference ships no model code; cfg5 is a caller built here",
+                       "decode": "the decode line is an addition of this build; the reference arm is the default config's",
+                       "cp": "the reference has no sequence parallelism; the reference arm is the default config's"
+                       }[args.config]
                 print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
             return
         cfg = None
@@ -512,8 +651,8 @@ def main():
             os.dup2(saved_fd, 1)
             os.close(saved_fd)
 
-    if args.config in ("cfg5", "decode"):
-        (run_gpt if args.config == "cfg5" else run_decode)(args, world, rank, local_rank, dev)
+    if args.config in ("cfg5", "decode", "cp"):
+        {"cfg5": run_gpt, "decode": run_decode, "cp": run_cp}[args.config](args, world, rank, local_rank, dev)
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()

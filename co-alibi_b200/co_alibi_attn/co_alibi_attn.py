@@ -165,7 +165,13 @@ def _bwd(q, k, v, o, do, lse, rowsig, slopes, causal, sm_scale, dA_carry_in=None
     stream = torch.cuda.current_stream(q.device).cuda_stream
     rec = kernel_events
     if dA_carry_in is not None:
+        if rec is not None:
+            e0, e1 = _ev(), _ev()
+            e0.record()
         _lib.check(lib.coalibi_bwd_carry(a, dA_carry_in.data_ptr(), stream), "coalibi_bwd_carry")
+        if rec is not None:
+            e1.record()
+            rec.setdefault("bwd_carry", []).append((e0, e1))
     elif rec is None:
         _lib.check(lib.coalibi_bwd(a, stream), "coalibi_bwd")
     else:

@@ -22,15 +22,16 @@ key shards c < r unmasked and shard r with the top-left mask.
 
 ``sequence_sharded_attention`` runs the shards one after another on one device
 (the building block, and its check); ``ring_attention`` gives every rank of a
-process group one sequence shard of q, k, v and passes key / value shards (and,
-in the backward, dk / dv accumulators) around the ring.
+process group chunks of the sequence (one contiguous shard, or two zig-zag
+chunks that balance the causal work) and passes key / value shards (and, in the
+backward, dk / dv accumulators) around the ring.
 """
 import torch
 import torch.distributed as dist
 
 from .co_alibi_attn import _api_slopes, _bwd, _check_inputs, _fwd
 
-__all__ = ["sequence_sharded_attention", "ring_attention"]
+__all__ = ["sequence_sharded_attention", "ring_attention", "chunk_layout"]
 
 
 def _kernel_fwd(q, k, v, slopes, causal, sm_scale):
@@ -156,75 +157,135 @@ def sequence_sharded_attention(q, k, v, n_shards, causal=True, sm_scale=None, bi
 
 
 # ---------------------------------------------------------------------------
-# ring over a process group: rank r holds sequence shard r of q, k, v
+# ring over a process group: every rank holds equal-length chunks of the sequence
 # ---------------------------------------------------------------------------
-def _ring_pass(tensors, group):
-    """Send ``tensors`` to the next rank, return the previous rank's."""
-    world, rank = dist.get_world_size(group), dist.get_rank(group)
-    nxt = dist.get_global_rank(group, (rank + 1) % world) if group is not None else (rank + 1) % world
-    prv = dist.get_global_rank(group, (rank - 1) % world) if group is not None else (rank - 1) % world
+def chunk_layout(layout, world, rank):
+    """Global chunk indices (in order) that ``rank`` holds.  "contiguous": the
+    sequence in ``world`` chunks, chunk r on rank r.  "zigzag": ``2 * world``
+    chunks, rank r holding chunks r and 2 * world - 1 - r, so that with causal
+    masking every rank has the same number of visible scores."""
+    if layout == "contiguous":
+        return [rank]
+    if layout == "zigzag":
+        return [rank, 2 * world - 1 - rank]
+    raise ValueError(f"unknown layout {layout!r} (contiguous or zigzag)")
+
+
+def _world_rank(group):
+    if group is None and not dist.is_initialized():
+        return 1, 0
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+def _ring_start(tensors, group):
+    """Start sending ``tensors`` to the next rank and receiving the previous
+    rank's; returns (receive buffers, requests)."""
+    world, rank = _world_rank(group)
+    glob = (lambda r: dist.get_global_rank(group, r)) if group is not None else (lambda r: r)
+    nxt, prv = glob((rank + 1) % world), glob((rank - 1) % world)
     recv = [torch.empty_like(t) for t in tensors]
     ops = [dist.P2POp(dist.isend, t, nxt, group) for t in tensors] + \
           [dist.P2POp(dist.irecv, t, prv, group) for t in recv]
-    for req in dist.batch_isend_irecv(ops):
-        req.wait()
+    return recv, dist.batch_isend_irecv(ops)
+
+
+def _finish(recv, reqs):
+    for r in reqs:
+        r.wait()
     return recv
+
+
+def _pieces(x, n):
+    L = x.shape[2] // n
+    return [x[:, :, i * L:(i + 1) * L] for i in range(n)]
 
 
 class _Ring(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, slopes, causal, sm_scale, group, fwd_fn, bwd_fn):
-        world, rank = dist.get_world_size(group), dist.get_rank(group)
-        m = _RowMerge(slopes)
+    def forward(ctx, q, k, v, slopes, causal, sm_scale, group, layout, fwd_fn, bwd_fn):
+        world, rank = _world_rank(group)
+        own = chunk_layout(layout, world, rank)
+        qc = dict(zip(own, _pieces(q, len(own))))
+        merges = {i: _RowMerge(slopes) for i in own}
         kv = [k, v]
         for s in range(world):
-            c = (rank - s) % world
-            if not (causal and c > rank):
-                m.add(c, *fwd_fn(q, kv[0], kv[1], slopes, causal and c == rank, sm_scale))
-            if s + 1 < world:
-                kv = _ring_pass(kv, group)
-        o, _, _ = m.finish(q.dtype)
+            src = (rank - s) % world
+            pending = _ring_start(kv, group) if s + 1 < world else None   # next shard, overlapped
+            for j, kj, vj in zip(chunk_layout(layout, world, src), _pieces(kv[0], len(own)), _pieces(kv[1], len(own))):
+                for i in own:
+                    if not (causal and j > i):
+                        merges[i].add(j, *fwd_fn(qc[i], kj, vj, slopes, causal and i == j, sm_scale))
+            if pending is not None:
+                kv = _finish(*pending)
+        o = torch.cat([merges[i].finish(q.dtype)[0] for i in own], dim=2)
         ctx.save_for_backward(q, k, v, o, slopes)
-        ctx.m, ctx.causal, ctx.sm_scale, ctx.group, ctx.bwd_fn = m, causal, sm_scale, group, bwd_fn
+        ctx.merges, ctx.causal, ctx.sm_scale, ctx.group, ctx.layout, ctx.bwd_fn = \
+            merges, causal, sm_scale, group, layout, bwd_fn
         return o
 
     @staticmethod
     def backward(ctx, do):
         q, k, v, o, slopes = ctx.saved_tensors
-        group, m, causal, scale = ctx.group, ctx.m, ctx.causal, ctx.sm_scale
-        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        group, merges, causal, scale, layout = ctx.group, ctx.merges, ctx.causal, ctx.sm_scale, ctx.layout
+        world, rank = _world_rank(group)
+        own = chunk_layout(layout, world, rank)
+        n = len(own)
         do = do.to(q.dtype).contiguous()
-        carry = m.carries(o, do)
-        acc = torch.promote_types(q.dtype, torch.float32)
-        dq = torch.zeros(q.shape, dtype=acc, device=q.device)
-        # key / value shard c travels with the float32 dk / dv accumulators of shard c
-        buf = [k, v, torch.zeros(k.shape, dtype=acc, device=k.device), torch.zeros(v.shape, dtype=acc, device=v.device)]
+        acc_t = torch.promote_types(q.dtype, torch.float32)
+        qc, oc, doc = (dict(zip(own, [t.contiguous() for t in _pieces(x, n)])) for x in (q, o, do))
+        carries = {i: merges[i].carries(oc[i], doc[i]) for i in own}
+        dq = {i: torch.zeros(qc[i].shape, dtype=acc_t, device=q.device) for i in own}
+        kv, acc, acc_pending = [k, v], None, None
         for s in range(world):
-            c = (rank - s) % world
-            if c in m.shifted:
-                o_c, lse_p, t_c, R = m.shifted[c]
-                g = ctx.bwd_fn(q, buf[0], buf[1], o, do, m.lse, t_c + R, slopes, causal and c == rank, scale,
-                               carry[c])
-                dq += g[0].to(acc)
-                buf[2] += g[1].to(acc)
-                buf[3] += g[2].to(acc)
-            buf = _ring_pass(buf, group) if s + 1 < world else _ring_pass(buf[2:], group)
-        # after `world` passes the accumulators of shard `rank` are back here
-        return dq.to(q.dtype), buf[0].to(k.dtype), buf[1].to(v.dtype), None, None, None, None, None, None
+            src = (rank - s) % world
+            kv_pending = _ring_start(kv, group) if s + 1 < world else None
+            gk = torch.zeros(k.shape, dtype=acc_t, device=k.device)
+            gv = torch.zeros(v.shape, dtype=acc_t, device=v.device)
+            for jj, (j, kj, vj) in enumerate(zip(chunk_layout(layout, world, src), _pieces(kv[0], n),
+                                                 _pieces(kv[1], n))):
+                L = kj.shape[2]
+                for i in own:
+                    if j not in merges[i].shifted:
+                        continue
+                    o_c, lse_p, t_c, R = merges[i].shifted[j]
+                    g = ctx.bwd_fn(qc[i], kj, vj, oc[i], doc[i], merges[i].lse, t_c + R, slopes,
+                                   causal and i == j, scale, carries[i][j])
+                    dq[i] += g[0].to(acc_t)
+                    gk[:, :, jj * L:(jj + 1) * L] += g[1].to(acc_t)
+                    gv[:, :, jj * L:(jj + 1) * L] += g[2].to(acc_t)
+            # the visiting shard's dk / dv accumulators arrive while its pairs computed
+            if acc_pending is not None:
+                acc = _finish(*acc_pending)
+                gk += acc[0]
+                gv += acc[1]
+            acc_pending = _ring_start([gk, gv], group) if world > 1 else ([gk, gv], [])
+            if kv_pending is not None:
+                kv = _finish(*kv_pending)
+        # after `world` passes the accumulators of this rank's own chunks are back here
+        dk, dv = _finish(*acc_pending)
+        dq = torch.cat([dq[i] for i in own], dim=2)
+        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), None, None, None, None, None, None, None
 
 
-def ring_attention(q, k, v, causal=True, sm_scale=None, bias_max=8.0, group=None, _shard_fns=None):
-    """Co-ALiBi attention over a sequence split across the ranks of ``group``:
-    rank r passes its contiguous shard r of q [B, Hq, S_r, D] and k, v
-    [B, Hkv, S_r, D] (all heads; equal shard lengths) and gets its rows of the
-    output, with gradients for its shards.  Key / value shards travel around the
-    ring; no rank holds the whole sequence.  ``_shard_fns`` (tests only) replaces
-    the per-shard kernels with a (forward, backward) pair of the same signature."""
+def ring_attention(q, k, v, causal=True, sm_scale=None, bias_max=8.0, group=None, layout="contiguous",
+                   _shard_fns=None):
+    """Co-ALiBi attention over a sequence split across the ranks of ``group``.
+    Rank r passes its chunks of q [B, Hq, S_r, D] and k, v [B, Hkv, S_r, D] (all
+    heads; every rank the same S_r), concatenated in the order ``chunk_layout``
+    gives -- one contiguous shard, or with ``layout="zigzag"`` chunks r and
+    2 * world - 1 - r of a sequence cut into 2 * world -- and gets its rows of the
+    output, with gradients for its chunks.  Key / value shards travel around the
+    ring, each send overlapped with the pairs computed on the shard before it; no
+    rank holds the whole sequence.  ``_shard_fns`` (tests only) replaces the
+    per-shard kernels with a (forward, backward) pair of the same signature."""
     if sm_scale is None:
         sm_scale = 1.0 / (q.shape[-1] ** 0.5)
     fwd_fn, bwd_fn = _shard_fns or (_kernel_fwd, _kernel_bwd)
     slopes = _api_slopes(q.shape[1], bias_max, q.dtype, q.device)
     if _shard_fns is None:
         _check_inputs(q, k, v, slopes)
-    return _Ring.apply(q.contiguous(), k.contiguous(), v.contiguous(), slopes, causal, sm_scale, group, fwd_fn,
-                       bwd_fn)
+    n = len(chunk_layout(layout, 1, 0))
+    if q.shape[2] % n or k.shape[2] != q.shape[2]:
+        raise ValueError(f"ring_attention: q and k / v need the same sequence length, a multiple of {n}")
+    return _Ring.apply(q.contiguous(), k.contiguous(), v.contiguous(), slopes, causal, sm_scale, group, layout,
+                       fwd_fn, bwd_fn)

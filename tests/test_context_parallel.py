@@ -125,38 +125,60 @@ def _collect(procs, qu, n, limit):
     return got
 
 
-def _ring_worker(rank, world, port, causal, out):
+def _local(x, layout, world, rank):
+    """This rank's chunks of x (sequence axis 2), in chunk_layout order."""
+    from co_alibi_attn.context_parallel import chunk_layout
+    own = chunk_layout(layout, world, rank)
+    n = world * len(own)
+    L = x.shape[2] // n
+    return torch.cat([x[:, :, i * L:(i + 1) * L] for i in own], dim=2)
+
+
+def _global(parts, layout, world):
+    """Inverse of _local over all ranks: the whole sequence from every rank's chunks."""
+    from co_alibi_attn.context_parallel import chunk_layout
+    chunks = {}
+    for r in range(world):
+        own = chunk_layout(layout, world, r)
+        L = parts[r].shape[2] // len(own)
+        for j, i in enumerate(own):
+            chunks[i] = parts[r][:, :, j * L:(j + 1) * L]
+    return torch.cat([chunks[i] for i in sorted(chunks)], dim=2)
+
+
+def _ring_worker(rank, world, port, causal, layout, out):
     import sys
     for p in (ROOT, os.path.join(ROOT, "co-alibi_b200")):
         if p not in sys.path:
             sys.path.insert(0, p)
+    import datetime
     from co_alibi_attn.context_parallel import ring_attention
-    from tests.test_context_parallel import STAND_INS
+    from tests.test_context_parallel import STAND_INS, _local
     from tests._common import make_inputs
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=__import__("datetime").timedelta(seconds=60))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         q, k, v, do = (t.double() for t in make_inputs(1, 4, 2, 12 * world, 12 * world, 8, torch.float32, seed=5))
-        sh = slice(12 * rank, 12 * (rank + 1))
-        ql, kl, vl = (t[:, :, sh].clone().requires_grad_(True) for t in (q, k, v))
-        o = ring_attention(ql, kl, vl, causal=causal, sm_scale=0.3, _shard_fns=STAND_INS)
-        o.backward(do[:, :, sh])
+        ql, kl, vl = (_local(t, layout, world, rank).requires_grad_(True) for t in (q, k, v))
+        o = ring_attention(ql, kl, vl, causal=causal, sm_scale=0.3, layout=layout, _shard_fns=STAND_INS)
+        o.backward(_local(do, layout, world, rank))
         out.put((rank, [t.detach().numpy().copy() for t in (o, ql.grad, kl.grad, vl.grad)]))
     finally:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("layout", ["contiguous", "zigzag"])
 @pytest.mark.parametrize("causal", [True, False])
-def test_ring_gloo_three_ranks_with_oracle_shards(causal):
-    """Three gloo ranks, one sequence shard each, key / value shards and dk / dv
-    accumulators passed around the ring: the concatenated outputs and gradients equal
-    the oracle on the whole sequence."""
+def test_ring_gloo_three_ranks_with_oracle_shards(causal, layout):
+    """Three gloo ranks, each with its chunks of the sequence, key / value shards and
+    dk / dv accumulators passed around the ring (sends overlapped with the pairs):
+    the reassembled outputs and gradients equal the oracle on the whole sequence."""
     world = 3
     ctx = mp.get_context("spawn")
     qu = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_ring_worker, args=(r, world, port, causal, qu)) for r in range(world)]
+    procs = [ctx.Process(target=_ring_worker, args=(r, world, port, causal, layout, qu)) for r in range(world)]
     for p in procs:
         p.start()
     got = _collect(procs, qu, world, 300)
@@ -164,8 +186,22 @@ def test_ring_gloo_three_ranks_with_oracle_shards(causal):
     ref = _whole(q, k, v, do, causal, 0.3)
     # worker order (o, dq, dk, dv); forward_backward order (o, lse, rowsig, dq, dk, dv)
     for j, (i, name) in enumerate(((0, "o"), (3, "dq"), (4, "dk"), (5, "dv"))):
-        x = torch.cat([torch.from_numpy(got[r][j]) for r in range(world)], dim=2)
+        x = _global([torch.from_numpy(got[r][j]) for r in range(world)], layout, world)
         assert (x - ref[i]).abs().max().item() < 1e-8, name
+
+
+def test_ring_without_process_group_is_one_rank():
+    """No process group: one rank holding the whole sequence (zig-zag: its two halves)."""
+    from co_alibi_attn.context_parallel import ring_attention
+    q, k, v, do = (t.double() for t in make_inputs(2, 4, 2, 40, 40, 8, torch.float32, seed=8))
+    q, k, v = (t.requires_grad_(True) for t in (q, k, v))
+    o = ring_attention(q, k, v, causal=True, sm_scale=0.3, layout="zigzag", _shard_fns=STAND_INS)
+    o.backward(do)
+    ref = _whole(q.detach(), k.detach(), v.detach(), do, True, 0.3)
+    for x, i in ((o.detach(), 0), (q.grad, 3), (k.grad, 4), (v.grad, 5)):
+        assert (x - ref[i]).abs().max().item() < 1e-8
+    with pytest.raises(ValueError):
+        ring_attention(q[:, :, :39], k[:, :, :39], v[:, :, :39], layout="zigzag", _shard_fns=STAND_INS)
 
 
 # --- GPU: the sm_100a shard kernels ------------------------------------------
@@ -208,6 +244,26 @@ def test_sharded_kernels_match_oracle(case):
     assert rel_err(qc.grad.cpu(), qu.grad.cpu()) < GRAD_REL
 
 
+@pytest.mark.gpu
+def test_ring_one_rank_zigzag_kernels_match_oracle():
+    """ring_attention without a process group (one rank, two zig-zag halves) on the
+    kernels: the code path of bench.py --config cp at N=1."""
+    import co_alibi_attn
+    from co_alibi_attn.context_parallel import ring_attention
+    q, k, v, do = make_inputs(1, 8, 2, 1024, 1024, 128, torch.bfloat16, seed=41)
+    scale = 1.0 / math.sqrt(128)
+    qc, kc, vc = (t.cuda().requires_grad_(True) for t in (q, k, v))
+    o = ring_attention(qc, kc, vc, causal=True, layout="zigzag")
+    o.backward(do.cuda())
+    torch.cuda.synchronize()
+    assert co_alibi_attn.device_status(reset=True) == 0
+    o_ref, _, _, pav = oracle_fwd_pv(q, k, v, True, scale)
+    ok, err = check_o(o.detach().cpu(), o_ref, torch.bfloat16, pav)
+    assert ok, f"O max-abs {err:.3e}"
+    for name, x, r in zip(("dq", "dk", "dv"), (qc.grad, kc.grad, vc.grad), oracle_bwd(q, k, v, do, True, scale)):
+        assert rel_err(x.cpu(), r) <= GRAD_REL, name
+
+
 def _nccl_ring_worker(rank, world, port, out):
     import sys
     for p in (ROOT, os.path.join(ROOT, "co-alibi_b200")):
@@ -223,12 +279,12 @@ def _nccl_ring_worker(rank, world, port, out):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
                             device_id=torch.device("cuda", rank))
     try:
+        from tests.test_context_parallel import _local
         S = 512 * world
         q, k, v, do = make_inputs(1, 8, 2, S, S, 128, torch.bfloat16, seed=31)
-        sh = slice(512 * rank, 512 * (rank + 1))
-        ql, kl, vl = (t[:, :, sh].cuda().requires_grad_(True) for t in (q, k, v))
-        o = ring_attention(ql, kl, vl, causal=True)
-        o.backward(do[:, :, sh].cuda())
+        ql, kl, vl = (_local(t, "zigzag", world, rank).cuda().requires_grad_(True) for t in (q, k, v))
+        o = ring_attention(ql, kl, vl, causal=True, layout="zigzag")
+        o.backward(_local(do, "zigzag", world, rank).cuda())
         torch.cuda.synchronize()
         out.put((rank, [t.detach().float().cpu().numpy().copy() for t in (o, ql.grad, kl.grad, vl.grad)]))
     finally:
@@ -237,7 +293,7 @@ def _nccl_ring_worker(rank, world, port, out):
 
 @pytest.mark.gpu
 def test_ring_nccl_matches_oracle():
-    """One sequence shard per GPU over NCCL (needs 2 or more GPUs)."""
+    """Zig-zag chunks on every GPU, the ring over NCCL (needs 2 or more GPUs)."""
     world = torch.cuda.device_count()
     if world < 2:
         pytest.skip("needs two GPUs")
@@ -252,7 +308,7 @@ def test_ring_nccl_matches_oracle():
     S = 512 * world
     q, k, v, do = make_inputs(1, 8, 2, S, S, 128, torch.bfloat16, seed=31)
     scale = 1.0 / math.sqrt(128)
-    cat = lambda i: torch.cat([torch.from_numpy(got[r][i]) for r in range(world)], dim=2)  # noqa: E731
+    cat = lambda i: _global([torch.from_numpy(got[r][i]) for r in range(world)], "zigzag", world)  # noqa: E731
     o_ref, _, _, pav = oracle_fwd_pv(q, k, v, True, scale)
     ok, err = check_o(cat(0).to(torch.bfloat16), o_ref, torch.bfloat16, pav)
     assert ok, f"O max-abs {err:.3e}"
