@@ -80,6 +80,7 @@ class ClockSampler:
         self.idx = gpu_index
         self.proc = None
         self.lines = []
+        self.base = 0
 
     def start(self):
         try:
@@ -89,6 +90,12 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # return once nvidia-smi is sampling, and count only the samples taken
+            # after this point (inside the timed region)
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.01)
+            self.base = len(self.lines)
         except Exception:
             self.proc = None
 
@@ -105,9 +112,18 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
         self.t.join(timeout=2)
+        lines = self.lines[self.base:]
+        if not lines:
+            # a timed region shorter than the sampling period: one reading right after it
+            try:
+                r = subprocess.run(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                    "-i", str(self.idx)], capture_output=True, text=True, timeout=10)
+                lines = [ln.strip() for ln in r.stdout.splitlines()]
+            except Exception:
+                lines = []
         mhz, maxes, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -167,6 +183,62 @@ def cpu_sample_tflops(cfg, rows, reps, threads=None):
     desc = (f"oracle (model.py maths) fp32 {'fwd' if fwd_only else 'fwd+bwd'} on one (b,h) slice, "
             f"query rows {off}..{S - 1} of S={S}, D={D}, median of {reps}")
     return flops / t / 1e12, t, nthreads, desc
+
+
+def flash_side_by_side(cfg, dev, steps, warmup):
+    """FlashAttention-2 (flash_attn_func, the library's kernels) on the config's
+    shape and inputs, as the reference's benchmark_flops.py:94-136 does optionally:
+    layout [B, S, H, D], same scale and mask, CUDA events around `steps` forward
+    calls and `steps` forward + backward steps.  A comparator only: it computes
+    softmax attention without the Co-ALiBi bias.  Returns a dict, or the reason it
+    could not run."""
+    B, Hq, Hkv, S, D, dtype, causal, std, fwd_only = cfg
+    try:
+        from flash_attn import flash_attn_func
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"flash_attn import failed: {type(e).__name__}: {e}"[:200]}
+    import flash_attn
+    g = torch.Generator().manual_seed(7)
+    q = (torch.randn(B, S, Hq, D, generator=g) * std).to(dtype).to(dev).requires_grad_(True)
+    k = (torch.randn(B, S, Hkv, D, generator=g) * std).to(dtype).to(dev).requires_grad_(True)
+    v = (torch.randn(B, S, Hkv, D, generator=g) * std).to(dtype).to(dev).requires_grad_(True)
+    do = torch.randn(B, S, Hq, D, generator=g).to(dtype).to(dev)
+    scale = 1.0 / math.sqrt(D)
+
+    def fwd():
+        with torch.no_grad():
+            flash_attn_func(q, k, v, softmax_scale=scale, causal=causal)
+
+    def fwd_bwd():
+        o = flash_attn_func(q, k, v, softmax_scale=scale, causal=causal)
+        o.backward(do)
+        q.grad = k.grad = v.grad = None
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    try:
+        fwd_ms = timed(fwd)
+        step_ms = None if fwd_only else timed(fwd_bwd)
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"flash_attn on this GPU: {type(e).__name__}: {e}"[:200]}
+    E = visible(S, causal) * B * Hq
+    out = {"impl": f"flash_attn {flash_attn.__version__} flash_attn_func (FlashAttention-2, softmax without the "
+                   f"Co-ALiBi bias)", "fwd_ms": round(fwd_ms, 4), "fwd_tflops": round(4.0 * D * E / fwd_ms / 1e9, 2)}
+    if step_ms is not None:
+        out.update({"fwd_bwd_ms": round(step_ms, 4), "fwd_bwd_tflops": round(14.0 * D * E / step_ms / 1e9, 2)})
+    del q, k, v, do
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_reference_arm(args, cfg, rank):
@@ -607,6 +679,8 @@ def main():
     ap.add_argument("--batch", type=int, default=None,
                     help="override the config's batch size (small cases for ncu captures)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-side-by-side", action="store_true",
+                    help="skip the FlashAttention-2 comparison on the same shape (N=1 only)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.config in ("cfg5", "decode", "cp"):
@@ -798,6 +872,10 @@ def main():
                     "(fwd 4D, pass A 6D, pass B 8D per score) / mean CUDA-event duration in the timed region; "
                     "second roofline: mufu_frac = MUFU ops per score (tanh + ex2 = 2, 1.75 where a quarter of the ex2 is a polynomial) / (16 ops/clk/SM x 148 SMs x sampled clock)"}
 
+    side = None
+    if world == 1 and not args.no_side_by_side:
+        side = flash_side_by_side(cfg, dev, max(3, min(args.steps, 50)), args.warmup)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tfl, tsec, nth, desc = cpu_sample_tflops(cfg, S, 3)
@@ -822,6 +900,7 @@ def main():
             "e2e": {"value": round(world * flops_step / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                     "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": kernels_per_step * args.steps, "clocks": clocks, "device_status": status,
+            "side_by_side": side,
         }
         print(json.dumps(line), flush=True)
 
