@@ -502,6 +502,10 @@ def run_cp(args, world, rank, local_rank, dev):
     import co_alibi_attn.co_alibi_attn as impl
     from co_alibi_attn.context_parallel import chunk_layout, ring_attention
     B, Hq, Hkv, S, D = CP_SHAPE
+    if args.seq_len:
+        S = args.seq_len
+        if S % (2 * world * 128):
+            raise SystemExit(f"--seq-len must be a multiple of {2 * world * 128} at N={world}")
     dt = torch.bfloat16
     own = chunk_layout("zigzag", world, rank)
     L = S // (2 * world)
@@ -596,13 +600,16 @@ def run_cp(args, world, rank, local_rank, dev):
                "seconds_per_sample": round(tsec, 3)}
     if rank == 0:
         line = {
-            "metric": metric_name("cp"), "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world,
+            "metric": metric_name("cp") if S == CP_SHAPE[3] else metric_name("cp").replace("S65536", f"S{S}"),
+            "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": f"cp: ring_attention fwd+bwd (context parallel, zig-zag chunks), B={B} Hq={Hq} "
                                    f"Hkv={Hkv} S={S} D={D} bf16 causal", "global_batch": B, "seq_len": S,
                        "parallelism": f"sequence x{world} ({2 * world} zig-zag chunks, NCCL ring)",
-                       "l2": "q, do (512 MiB each at N=1) exceed the 126 MB L2; no flush needed"},
+                       "l2": f"q, do ({q.numel() * 2 >> 20} MiB each on this rank) "
+                             + ("exceed the 126 MB L2; no flush needed" if q.numel() * 2 > 126e6 else
+                                "fit the 126 MB L2: a capture size, not a bench line")},
             "roofline": {"bound": "tensor", "kernel": "fwd + bwd_carry pair kernels (rank 0)", "achieved": round(ach, 2),
                          "peak": sustained, "unit": "TFLOP/s", "frac": round(ach / sustained, 4),
                          "peak_source": f"{peak_src} bf16_tflops_sustained", "traffic": None,
@@ -678,6 +685,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--batch", type=int, default=None,
                     help="override the config's batch size (small cases for ncu captures)")
+    ap.add_argument("--seq-len", type=int, default=None,
+                    help="--config cp only: override the sequence length (small cases for ncu captures)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-side-by-side", action="store_true",
                     help="skip the FlashAttention-2 comparison on the same shape (N=1 only)")
