@@ -43,9 +43,18 @@ def _kernel_bwd(q, k, v, o, do, lse, rowsig, slopes, causal, sm_scale, carry_in)
                 slopes, causal, sm_scale, dA_carry_in=carry_in.contiguous())
 
 
+def _acc(dtype):
+    """float32 for the merge arithmetic and accumulators (float64 kept, for float64 stand-ins)."""
+    return torch.promote_types(dtype, torch.float32)
+
+
 def _f(x):
-    """float32 for the merge arithmetic (float64 kept, for float64 stand-ins)."""
-    return x if x.dtype == torch.float64 else x.float()
+    return x if x.dtype == _acc(x.dtype) else x.float()
+
+
+def _dot(a, b):
+    """Row dot products over D in the accumulator precision (one converted copy)."""
+    return a.to(_acc(a.dtype), copy=True).mul_(b).sum(-1)
 
 
 class _RowMerge:
@@ -70,10 +79,10 @@ class _RowMerge:
             lse_p = lse_c - self.sl.to(lse_c.dtype) * R
             self.shifted[c] = (o_c, lse_p, t_c, R)
             if lse_all is None:
-                lse_all, o_all = lse_p, _f(o_c)
+                lse_all, o_all = lse_p, o_c.to(_acc(o_c.dtype), copy=True)
             else:
                 new = torch.logaddexp(lse_all, lse_p)
-                o_all = o_all * torch.exp(lse_all - new).unsqueeze(-1) + _f(o_c) * torch.exp(lse_p - new).unsqueeze(-1)
+                o_all.mul_(torch.exp(lse_all - new).unsqueeze(-1)).addcmul_(o_c, torch.exp(lse_p - new).unsqueeze(-1))
                 lse_all = new
             R = R + t_c
         self.lse, self.rowsig = lse_all, R
@@ -81,13 +90,13 @@ class _RowMerge:
 
     def carries(self, o, do):
         """dA carry-in C_c of every shard (left to right) for the row's O and dO."""
-        delta = (_f(do) * _f(o)).sum(-1)
+        delta = _dot(do, o)
         C, out = torch.zeros_like(delta), {}
         for c in sorted(self.shifted):
             o_c, lse_p, t_c, R = self.shifted[c]
             out[c] = C
             w = torch.exp(lse_p - self.lse)
-            C = C + w * ((_f(do) * _f(o_c)).sum(-1) - delta)
+            C = C + w * (_dot(do, o_c) - delta)
         return out
 
 
@@ -135,9 +144,9 @@ class _SequenceSharded(torch.autograd.Function):
             for c, (o_c, lse_p, t_c, R) in m.shifted.items():
                 g = ctx.bwd_fn(qs[r], ks[c], vs[c], o_r, do_r, m.lse, t_c + R, slopes, causal and c == r, scale,
                                carry[c])
-                dq[r] += g[0].to(acc)
-                dk[c] += g[1].to(acc)
-                dv[c] += g[2].to(acc)
+                dq[r].add_(g[0])
+                dk[c].add_(g[1])
+                dv[c].add_(g[2])
         cat = lambda xs, t: torch.cat(xs, dim=2).to(t.dtype)  # noqa: E731
         return cat(dq, q), cat(dk, k), cat(dv, v), None, None, None, None, None, None
 
@@ -250,14 +259,14 @@ class _Ring(torch.autograd.Function):
                     o_c, lse_p, t_c, R = merges[i].shifted[j]
                     g = ctx.bwd_fn(qc[i], kj, vj, oc[i], doc[i], merges[i].lse, t_c + R, slopes,
                                    causal and i == j, scale, carries[i][j])
-                    dq[i] += g[0].to(acc_t)
-                    gk[:, :, jj * L:(jj + 1) * L] += g[1].to(acc_t)
-                    gv[:, :, jj * L:(jj + 1) * L] += g[2].to(acc_t)
+                    dq[i].add_(g[0])
+                    gk[:, :, jj * L:(jj + 1) * L].add_(g[1])
+                    gv[:, :, jj * L:(jj + 1) * L].add_(g[2])
             # the visiting shard's dk / dv accumulators arrive while its pairs computed
             if acc_pending is not None:
                 acc = _finish(*acc_pending)
-                gk += acc[0]
-                gv += acc[1]
+                gk.add_(acc[0])
+                gv.add_(acc[1])
             acc_pending = _ring_start([gk, gv], group) if world > 1 else ([gk, gv], [])
             if kv_pending is not None:
                 kv = _finish(*kv_pending)
