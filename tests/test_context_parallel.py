@@ -211,6 +211,7 @@ GPU_CASES = [
     (2, 8, 2, 700, 64, 3, False, torch.bfloat16),     # GQA, ragged shards
     (1, 8, 2, 1000, 128, 2, True, torch.bfloat16),
     (1, 2, 2, 64, 128, 5, True, torch.float16),       # 13-row shards: the decode forward per shard
+    (1, 6, 3, 777, 64, 3, True, torch.float16),       # D = 64 pass B with a carry, causal, GQA, 259-row shards
 ]
 
 
