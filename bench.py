@@ -241,6 +241,36 @@ def flash_side_by_side(cfg, dev, steps, warmup):
     return out
 
 
+def pcie_copy_floor_ms(ins_h, outs_h, dev, reps=3):
+    """Time of the e2e step's transfers alone: every input copied host -> device on
+    one stream while every output is copied device -> host on another (both PCIe
+    directions at once), no kernels; the floor under the e2e number."""
+    ins_d = [torch.empty_like(h, device=dev) for h in ins_h]
+    outs_d = [torch.empty_like(h, device=dev) for h in outs_h]
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    cur = torch.cuda.current_stream(dev)
+    best = float("inf")
+    for _ in range(reps + 1):
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cur)
+        s_in.wait_stream(cur)
+        s_out.wait_stream(cur)
+        with torch.cuda.stream(s_in):
+            for d, h in zip(ins_d, ins_h):
+                d.copy_(h, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            for h, d in zip(outs_h, outs_d):
+                h.copy_(d, non_blocking=True)
+        cur.wait_stream(s_in)
+        cur.wait_stream(s_out)
+        e1.record(cur)
+        torch.cuda.synchronize(dev)
+        best = min(best, e0.elapsed_time(e1))
+    del ins_d, outs_d
+    return best
+
+
 def run_reference_arm(args, cfg, rank):
     if rank != 0:
         return
@@ -854,6 +884,7 @@ def main():
     e2e_ms = t.item()
     h2d = sum(x.numel() * x.element_size() for x in ([q_h, k_h, v_h] + ([] if fwd_only else [do_h])))
     d2h = sum(x.numel() * x.element_size() for x in outs_h)
+    copy_ms = pcie_copy_floor_ms([q_h, k_h, v_h] + ([] if fwd_only else [do_h]), outs_h, dev)
 
     # ---------------- roofline of the dominant kernel
     burst, sustained, hbm, peak_src = load_peaks()
@@ -907,7 +938,11 @@ def main():
                 / (ms_max * 1e-3) / 1e12, 3),
             "kernels": kernels, "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": round(world * flops_step / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
-                    "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                    "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "copy_only_ms": round(copy_ms, 3),
+                    "copy_only_frac": round(copy_ms / e2e_ms, 4),
+                    "note": "copy_only_ms: the same bytes copied host->device and device->host at once (pinned "
+                            "buffers, two streams, no kernels); e2e can be no faster"},
             "gpu_launches": kernels_per_step * args.steps, "clocks": clocks, "device_status": status,
             "side_by_side": side,
         }

@@ -15,7 +15,7 @@ import torch
 
 from .co_alibi_attn import _api_slopes, _bwd, _check_inputs, _fwd
 
-__all__ = ["co_alibi_attention_from_host"]
+__all__ = ["co_alibi_attention_from_host", "chunk_plan"]
 
 # One (copy-in, compute, copy-out) stream triple per device, reused by every call:
 # the caching allocator keeps freed blocks per stream, so fresh streams on each
@@ -45,6 +45,35 @@ def _check_host(name, t, dtype):
         raise ValueError(f"{name} must be contiguous")
 
 
+def chunk_plan(B, Hkv, chunks):
+    """The pieces a host batch goes through the device in: (batch element, kv heads
+    [g0, g1)) triples covering every (b, kv head) unit once, in memory order.
+    Pieces hold about m = B * Hkv / chunks kv heads (at most one batch element);
+    from 4 chunks up the first batch element starts with pieces of 1, 2, 4, ...
+    heads and the last one ends with them, so that the pipeline fills after a small copy-in and drains
+    after a small kernel and copy-out.  A piece never crosses a batch element."""
+    m = max(1, min(Hkv, -(-(B * Hkv) // chunks)))
+    ramp = []
+    while chunks >= 4 and (2 * ramp[-1] if ramp else 1) < m:
+        ramp.append(2 * ramp[-1] if ramp else 1)
+
+    def split(n):  # n heads in about n / m near-equal pieces
+        k = max(1, round(n / m))
+        return [n // k + (1 if i < n % k else 0) for i in range(k)] if n else []
+
+    units = []
+    for b in range(B):
+        pre = ramp if b == 0 else []
+        post = ramp[::-1] if b == B - 1 else []
+        if sum(pre) + sum(post) > Hkv:
+            pre, post = ([], []) if B > 1 or sum(ramp) > Hkv else (ramp, [])
+        g = 0
+        for sz in pre + split(Hkv - sum(pre) - sum(post)) + post:
+            units.append((b, g, g + sz))
+            g += sz
+    return units
+
+
 def co_alibi_attention_from_host(q, k, v, do=None, causal=True, sm_scale=None, bias_max=8.0, out=None,
                                  device=None, slopes=None, chunks=16):
     """Co-ALiBi attention of host tensors, streamed through one GPU.
@@ -56,8 +85,9 @@ def co_alibi_attention_from_host(q, k, v, do=None, causal=True, sm_scale=None, b
     ``out`` is given (a tuple of the same shapes, CPU tensors) the results are
     written there.  ``slopes`` (optional, [Hq]) replaces the slope table of
     ``co_alibi_attention`` (for instance the global-head slopes of a head shard).
-    The batch goes through the device in about ``chunks`` pieces.  The call
-    returns once the results are in host memory.
+    The batch goes through the device in about ``chunks`` pieces of (batch
+    element, kv-head range), smaller at the start and the end (``chunk_plan``).
+    The call returns once the results are in host memory.
     """
     _check_host("q", q, q.dtype)
     _check_host("k", k, q.dtype)
@@ -87,10 +117,8 @@ def co_alibi_attention_from_host(q, k, v, do=None, causal=True, sm_scale=None, b
     if sm_scale is None:
         sm_scale = 1.0 / (q.shape[-1] ** 0.5)
     G = Hq // Hkv
-    # chunk = (batch element, kv heads [g0, g1)); kv heads per chunk so that B * pieces ~ chunks
-    per_b = max(1, min(Hkv, -(-chunks // B)))
-    gstep = -(-Hkv // per_b)
-    units = [(b, g0, min(Hkv, g0 + gstep)) for b in range(B) for g0 in range(0, Hkv, gstep)]
+    units = chunk_plan(B, Hkv, chunks)
+    gstep = max(g1 - g0 for _, g0, g1 in units)
     n = len(units)
     ins = [q, k, v] + ([] if do is None else [do])
     with torch.cuda.device(dev):

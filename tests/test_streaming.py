@@ -8,6 +8,20 @@ import torch
 from tests._common import make_inputs
 
 
+@pytest.mark.parametrize("B,Hkv,chunks", [(8, 16, 16), (1, 1, 16), (2, 8, 16), (4, 8, 1), (3, 5, 7),
+                                          (8, 16, 32), (1, 12, 4), (1, 32, 16), (2, 2, 16)])
+def test_chunk_plan_covers_every_unit_in_order(B, Hkv, chunks):
+    from co_alibi_attn.streaming import chunk_plan
+    units = chunk_plan(B, Hkv, chunks)
+    assert all(0 <= g0 < g1 <= Hkv for _, g0, g1 in units)
+    assert [(b, g) for b, g0, g1 in units for g in range(g0, g1)] == [(b, g) for b in range(B) for g in range(Hkv)]
+    m = max(1, min(Hkv, -(-(B * Hkv) // chunks)))
+    assert max(g1 - g0 for _, g0, g1 in units) <= 2 * m
+    if chunks >= 4 and m > 1:
+        # small pieces first and last: the pipeline's fill and drain
+        assert units[0][2] - units[0][1] == 1 and units[-1][2] - units[-1][1] == 1
+
+
 def test_streaming_rejects_bad_arguments_on_cpu():
     from co_alibi_attn.streaming import co_alibi_attention_from_host
     q, k, v, do = make_inputs(2, 4, 2, 64, 64, 64, torch.float16)
