@@ -91,6 +91,20 @@ def test_sharded_merge_is_exact_with_oracle_shards(shape):
         assert rel_err(x, r) < 1e-8, name
 
 
+def test_sharded_non_causal_different_query_and_key_lengths():
+    """Non-causal rows need no shared boundaries: 30 query rows in 3 shards against
+    70 keys in 3 shards of 24, 24 and 22."""
+    from co_alibi_attn.context_parallel import sequence_sharded_attention
+    q, k, v, do = (t.double() for t in make_inputs(2, 4, 2, 30, 70, 8, torch.float32, seed=12))
+    q, k, v = (t.requires_grad_(True) for t in (q, k, v))
+    o = sequence_sharded_attention(q, k, v, 3, causal=False, sm_scale=0.4, _shard_fns=STAND_INS)
+    o.backward(do)
+    o_r, _, _, dq_r, dk_r, dv_r = _whole(q.detach(), k.detach(), v.detach(), do, False, 0.4)
+    assert (o.detach() - o_r).abs().max().item() < 1e-8
+    for name, x, r in (("dq", q.grad, dq_r), ("dk", k.grad, dk_r), ("dv", v.grad, dv_r)):
+        assert rel_err(x, r) < 1e-8, name
+
+
 def test_sharded_causal_needs_matching_boundaries():
     from co_alibi_attn.context_parallel import sequence_sharded_attention
     q, k, v, _ = (t.double() for t in make_inputs(1, 2, 2, 20, 30, 8, torch.float32))
@@ -213,6 +227,25 @@ GPU_CASES = [
     (1, 2, 2, 64, 128, 5, True, torch.float16),       # 13-row shards: the decode forward per shard
     (1, 6, 3, 777, 64, 3, True, torch.float16),       # D = 64 pass B with a carry, causal, GQA, 259-row shards
 ]
+
+
+@pytest.mark.gpu
+def test_sharded_kernels_non_causal_rectangular():
+    """Non-causal, 300 query rows against 1000 keys, 4 shards each side (GQA, bf16)."""
+    import co_alibi_attn
+    from co_alibi_attn.context_parallel import sequence_sharded_attention
+    q, k, v, do = make_inputs(1, 8, 2, 300, 1000, 128, torch.bfloat16, seed=77)
+    scale = 1.0 / math.sqrt(128)
+    qc, kc, vc = (t.cuda().requires_grad_(True) for t in (q, k, v))
+    o = sequence_sharded_attention(qc, kc, vc, 4, causal=False, sm_scale=scale)
+    o.backward(do.cuda())
+    torch.cuda.synchronize()
+    assert co_alibi_attn.device_status(reset=True) == 0
+    o_ref, _, _, pav = oracle_fwd_pv(q, k, v, False, scale)
+    ok, err = check_o(o.detach().cpu(), o_ref, torch.bfloat16, pav)
+    assert ok, f"O max-abs {err:.3e}"
+    for name, x, r in zip(("dq", "dk", "dv"), (qc.grad, kc.grad, vc.grad), oracle_bwd(q, k, v, do, False, scale)):
+        assert rel_err(x.cpu(), r) <= GRAD_REL, name
 
 
 @pytest.mark.gpu
