@@ -204,6 +204,17 @@ def test_ring_gloo_three_ranks_with_oracle_shards(causal, layout):
         assert (x - ref[i]).abs().max().item() < 1e-8, name
 
 
+def test_chunk_layouts():
+    from co_alibi_attn.context_parallel import chunk_layout
+    assert [chunk_layout("contiguous", 4, r) for r in range(4)] == [[0], [1], [2], [3]]
+    zz = [chunk_layout("zigzag", 4, r) for r in range(4)]
+    assert zz == [[0, 7], [1, 6], [2, 5], [3, 4]]
+    # causal work per rank (visible chunk pairs, diagonal counted as 1/2) is equal under zig-zag
+    assert len({sum(i + 0.5 for i in own) for own in zz}) == 1
+    with pytest.raises(ValueError):
+        chunk_layout("striped", 4, 0)
+
+
 def test_ring_without_process_group_is_one_rank():
     """No process group: one rank holding the whole sequence (zig-zag: its two halves)."""
     from co_alibi_attn.context_parallel import ring_attention
