@@ -42,7 +42,7 @@ class CoalibiBwdArgs(ctypes.Structure):
 EXPORTS = ("coalibi_fwd", "coalibi_fwd_decode", "coalibi_fwd_decode_workspace_bytes", "coalibi_bwd",
            "coalibi_bwd_carry", "coalibi_bwd_phases", "coalibi_bwd_noalloc",
            "coalibi_bwd_workspace_bytes", "coalibi_selftest_wait_timeout", "coalibi_strerror",
-           "coalibi_abi_version", "coalibi_last_error")
+           "coalibi_abi_version", "coalibi_last_error", "coalibi_describe_launch")
 
 NOALLOC_SCRATCH_BYTES = 64 << 20  # COALIBI_NOALLOC_SCRATCH_BYTES
 
@@ -84,10 +84,23 @@ def load():
             lib.coalibi_strerror.restype = ctypes.c_char_p
             lib.coalibi_last_error.argtypes = []
             lib.coalibi_last_error.restype = ctypes.c_char_p
+            lib.coalibi_describe_launch.argtypes = [c_int] * 8 + [ctypes.c_char_p, c_size_t]
+            lib.coalibi_describe_launch.restype = c_int
             lib.coalibi_abi_version.argtypes = []
             lib.coalibi_abi_version.restype = c_int
             _lib = lib
     return _lib
+
+
+FWD, DECODE, BWD = 0, 1, 2  # `which` of coalibi_describe_launch
+
+
+def describe_launch(which: int, B: int, Hq: int, Hkv: int, Sq: int, Skv: int, D: int, device: int) -> str:
+    """The library's launch configuration for a problem, as text (coalibi_describe_launch)."""
+    buf = ctypes.create_string_buffer(512)
+    check(load().coalibi_describe_launch(which, B, Hq, Hkv, Sq, Skv, D, device, buf, len(buf)),
+          "coalibi_describe_launch")
+    return buf.value.decode()
 
 
 def strerror(code: int) -> str:

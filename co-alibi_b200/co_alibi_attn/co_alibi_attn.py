@@ -11,6 +11,7 @@ Differences from the reference, all invisible to callers:
   instead of being copied host-to-device on every call (reference :147).
 """
 import math
+import os
 import threading
 
 import torch
@@ -100,6 +101,14 @@ def _check_inputs(q, k, v, slopes):
         raise TypeError(f"co_alibi_attn: slopes must be float16/bfloat16/float32, got {slopes.dtype}")
 
 
+def _verbose(which, B, Hq, Hkv, Sq, Skv, D, device):
+    """With COALIBI_VERBOSE=1, print the launch configuration of each call, as the
+    reference prints its autotuned configs (co_alibi_attn/co_alibi_attn.py:58-63,
+    :125-130)."""
+    if os.getenv("COALIBI_VERBOSE", "0") == "1":
+        print(f"[Co-ALIBI] {_lib.describe_launch(which, B, Hq, Hkv, Sq, Skv, D, device.index)}")
+
+
 # Sq limit of coalibi_fwd_decode (COALIBI_DECODE_MAX_SQ in coalibi.h)
 DECODE_MAX_SQ = 16
 
@@ -138,6 +147,7 @@ def _fwd(q, k, v, slopes, causal, sm_scale, decode=None):
     if rec is not None:
         e1.record()
         rec.setdefault("fwd", []).append((e0, e1))
+    _verbose(_lib.DECODE if decode else _lib.FWD, B, Hq, Hkv, Sq, Skv, D, q.device)
     return o, lse, rowsig
 
 
@@ -181,6 +191,7 @@ def _bwd(q, k, v, o, do, lse, rowsig, slopes, causal, sm_scale, dA_carry_in=None
             _lib.check(lib.coalibi_bwd_phases(a, bit, stream), "coalibi_bwd_phases")
             e1.record()
             rec.setdefault(name, []).append((e0, e1))
+    _verbose(_lib.BWD, B, Hq, Hkv, Sq, Skv, D, q.device)
     return dq, dk, dv
 
 

@@ -11,6 +11,7 @@
 #include <mutex>
 
 #include "coalibi.h"
+#include "ctx_guard.h"
 #include "fwd.cuh"
 #include "decode.cuh"
 #include "bwd.cuh"
@@ -136,6 +137,64 @@ int device_setup(const void* ptr) {
   return st.status;
 }
 
+}  // namespace
+
+// Driver entry points for saving / restoring the thread's current context (the
+// runtime API has no call that makes "no context" current again).
+struct CtxFns {
+  PFN_cuCtxGetCurrent_v4000 get = nullptr;
+  PFN_cuCtxSetCurrent_v4000 set = nullptr;
+};
+
+static const CtxFns& ctx_fns() {
+  static CtxFns fns;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fns.get = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxSetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fns.set = reinterpret_cast<PFN_cuCtxSetCurrent_v4000>(p);
+  });
+  return fns;
+}
+
+CtxGuard::CtxGuard() {
+  const CtxFns& f = ctx_fns();
+  if (f.get != nullptr && f.set != nullptr) saved_ok_ = f.get(&saved_) == CUDA_SUCCESS;
+}
+
+CtxGuard::~CtxGuard() {
+  if (!saved_ok_) return;
+  CUcontext now = nullptr;
+  const CtxFns& f = ctx_fns();
+  if (f.get(&now) == CUDA_SUCCESS && now == saved_) return;
+  f.set(saved_);
+}
+
+int enter_device(const void* ptr, void* stream) {
+  if (int rc = device_setup(ptr)) return rc;
+  int dev = -1, sdev = -1;
+  cudaGetDevice(&dev);
+  if (cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev) != cudaSuccess) {
+    cudaGetLastError();
+    snprintf(g_last_error, sizeof(g_last_error), "cudaStreamGetDevice failed for stream %p", stream);
+    return COALIBI_ERR_DEVICE;
+  }
+  if (sdev != dev) {
+    snprintf(g_last_error, sizeof(g_last_error),
+             "stream %p belongs to device %d but the tensors are on device %d", stream, sdev, dev);
+    return COALIBI_ERR_DEVICE;
+  }
+  return COALIBI_OK;
+}
+
+namespace {
+
 // SM count of the current device (device_setup has run for it)
 int current_sm_count() {
   int dev = 0;
@@ -144,6 +203,8 @@ int current_sm_count() {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
 
 int check_common(int B, int Hq, int Hkv, int Sq, int Skv, int D, int dtype, int slopes_dtype) {
   if (D != 64 && D != 128) return COALIBI_ERR_HEAD_DIM;
@@ -157,6 +218,8 @@ int check_common(int B, int Hq, int Hkv, int Sq, int Skv, int D, int dtype, int 
   if ((long long)B * Hq > 0x7fffffffLL || (long long)B * Hkv * Skv > (1LL << 40)) return COALIBI_ERR_SHAPE;
   return COALIBI_OK;
 }
+
+namespace {
 
 unsigned long long timeout_ns(unsigned ms) {
   return (unsigned long long)(ms == 0 ? kDefaultTimeoutMs : ms) * 1000000ull;
@@ -215,7 +278,8 @@ using namespace coalibi;
 
 extern "C" int coalibi_selftest_wait_timeout(unsigned int timeout_ms, int* status, void* stream) {
   if (status == nullptr) return COALIBI_ERR_NULL_POINTER;
-  if (int rc = device_setup(status)) return rc;
+  CtxGuard guard;
+  if (int rc = enter_device(status, stream)) return rc;
   selftest_wait_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(status, timeout_ns(timeout_ms));
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -231,7 +295,8 @@ extern "C" int coalibi_fwd(const CoalibiFwdArgs* a, void* stream) {
   int rc = check_common(a->B, a->Hq, a->Hkv, a->Sq, a->Skv, a->D, a->dtype, a->slopes_dtype);
   if (rc) return rc;
   if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o)) return COALIBI_ERR_ALIGNMENT;
-  if ((rc = device_setup(a->q))) return rc;
+  CtxGuard guard;
+  if ((rc = enter_device(a->q, stream))) return rc;
   const bool bf16 = a->dtype == COALIBI_BF16;
   CUtensorMap tq, tk, tv;
   if ((rc = make_tmap(&tq, a->q, a->D, a->Sq, a->B * a->Hq, 128, bf16))) return rc;
@@ -302,7 +367,8 @@ extern "C" int coalibi_fwd_decode(const CoalibiFwdArgs* a, void* workspace, size
   if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o)) return COALIBI_ERR_ALIGNMENT;
   const size_t need = coalibi_fwd_decode_workspace_bytes(a->B, a->Hq, a->Hkv, a->Sq, a->Skv, a->D);
   if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)) return COALIBI_ERR_WORKSPACE;
-  if ((rc = device_setup(a->q))) return rc;
+  CtxGuard guard;
+  if ((rc = enter_device(a->q, stream))) return rc;
   DecodeParams p{};
   p.q = a->q;
   p.k = a->k;
@@ -352,7 +418,8 @@ extern "C" int coalibi_bwd_phases(const CoalibiBwdArgs* a, int phase_mask, void*
   const BwdWorkspace ws = bwd_workspace_layout(a->B, a->Hq, a->Sq, a->Skv);
   if (a->workspace == nullptr || a->workspace_bytes < ws.total) return COALIBI_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0) return COALIBI_ERR_ALIGNMENT;
-  if ((rc = device_setup(a->q))) return rc;
+  CtxGuard guard;
+  if ((rc = enter_device(a->q, stream))) return rc;
   return bwd_launch(*a, ws, timeout_ns(a->timeout_ms), static_cast<cudaStream_t>(stream), phase_mask);
 }
 
@@ -371,8 +438,58 @@ extern "C" int coalibi_bwd_carry(const CoalibiBwdArgs* a, const float* dA_carry_
   const BwdWorkspace ws = bwd_workspace_layout(a->B, a->Hq, a->Sq, a->Skv);
   if (a->workspace == nullptr || a->workspace_bytes < ws.total) return COALIBI_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0) return COALIBI_ERR_ALIGNMENT;
-  if ((rc = device_setup(a->q))) return rc;
+  CtxGuard guard;
+  if ((rc = enter_device(a->q, stream))) return rc;
   return bwd_launch(*a, ws, timeout_ns(a->timeout_ms), static_cast<cudaStream_t>(stream), 7, dA_carry_in);
+}
+
+extern "C" int coalibi_describe_launch(int which, int B, int Hq, int Hkv, int Sq, int Skv, int D, int device,
+                                       char* buf, size_t buf_len) {
+  if (buf == nullptr || buf_len == 0) return COALIBI_ERR_NULL_POINTER;
+  buf[0] = '\0';
+  CtxGuard guard;
+  if (int rc = check_common(B, Hq, Hkv, Sq, Skv, D, COALIBI_F16, COALIBI_F32)) return rc;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || sms <= 0) {
+    cudaGetLastError();
+    return COALIBI_ERR_DEVICE;
+  }
+  const int nq = (Sq + 127) / 128;
+  if (which == 0) {
+    // the rule of launch_fwd_impl
+    const long long items = (long long)B * Hq * nq;
+    const bool persistent = items >= 12LL * sms;
+    const int threads = D == 128 ? FwdLayout<128>::THREADS : FwdLayout<64>::THREADS;
+    const int smem = D == 128 ? FwdLayout<128>::ALLOC : FwdLayout<64>::ALLOC;
+    snprintf(buf, buf_len,
+             "forward coalibi_fwd_kernel<D=%d>: %s grid of %lld CTAs over %lld (head, 128-row query tile) items, "
+             "%d threads, %d B shared memory, 128-key tiles",
+             D, persistent ? "persistent (one CTA per SM, snake order)" : "one item per CTA",
+             persistent ? (long long)sms : items, items, threads, smem);
+    return COALIBI_OK;
+  }
+  if (which == 1) {
+    if (Sq > kDecodeMaxSq) return COALIBI_ERR_SHAPE;
+    const DecodePlan pl = D == 128 ? decode_plan<128>(B, Hq, Hkv, Sq, Skv) : decode_plan<64>(B, Hq, Hkv, Sq, Skv);
+    const int step = (D == 64 || pl.n_rgroups > 1) ? 16 : 32;  // the rule of launch_decode
+    snprintf(buf, buf_len,
+             "decode coalibi_decode_mma_kernel<D=%d, %d-key steps>: grid (%d, %d, %d) of 128 threads, %d keys per "
+             "CTA chunk, %d row groups; then coalibi_decode_combine_kernel over %lld query rows",
+             D, step, B * Hkv, pl.records / 4, pl.n_rgroups, pl.chunk_keys, pl.n_rgroups, (long long)B * Hq * Sq);
+    return COALIBI_OK;
+  }
+  if (which == 2) {
+    const int kb = D == 128 ? BwdB128Layout::KB : BwdBLayout<64>::KB;
+    const long long nb = (Skv + kb - 1) / kb;
+    snprintf(buf, buf_len,
+             "backward: coalibi_bwd_delta_kernel<D=%d>; coalibi_bwd_a_kernel<D=%d> (query-major) grid %lld x %d "
+             "threads; %s (key-major, %d keys per CTA, GQA group of %d heads summed in TMEM) grid %lld x %d threads",
+             D, D, (long long)B * Hq * nq, D == 128 ? BwdALayout<128>::THREADS : BwdALayout<64>::THREADS,
+             D == 128 ? "coalibi_bwd_b128_kernel" : "coalibi_bwd_b_kernel<D=64>", kb, Hq / Hkv,
+             (long long)B * Hkv * nb, D == 128 ? BwdB128Layout::THREADS : BwdBLayout<64>::THREADS);
+    return COALIBI_OK;
+  }
+  return COALIBI_ERR_SHAPE;
 }
 
 extern "C" const char* coalibi_strerror(int code) {

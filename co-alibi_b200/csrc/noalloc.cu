@@ -8,9 +8,9 @@
 // synchronise the whole device and, inside a process whose memory is managed by
 // a caching allocator, competes with it for the same pool.
 //
-// The backward's scratch (the per-row delta and the per-64-key carries pass A
-// hands to pass B) lives in kNoallocScratchBytes of file-scope __device__
-// memory.  Every GPU that loads this library holds that much memory until the
+// The backward's scratch (the per-row delta and the per-32-key carries -- z
+// suffix and dA prefix -- that pass A hands to pass B) lives in
+// kNoallocScratchBytes of file-scope __device__ memory.  Every GPU that loads this library holds that much memory until the
 // process exits.  Problems whose scratch would exceed it are rejected with
 // COALIBI_ERR_WORKSPACE before anything is launched.
 //
@@ -21,8 +21,13 @@
 // corrupt each other's results: serialise them.
 //
 // The device address of the array is looked up with cudaGetSymbolAddress once
-// per device, with that device current, by the first call made on that device.
-// Make that first call before any stream capture begins.
+// per device, with that device current, by the first call made on that device
+// (a failed lookup is not remembered: the next call tries again).  Make that
+// first call before any stream capture begins.  The address is not looked up
+// again afterwards, so it is stale after cudaDeviceReset on that device.
+//
+// Like every entry point of the library, the call leaves the calling thread's
+// current CUDA context as it found it.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -30,9 +35,11 @@
 #include <mutex>
 
 #include "coalibi.h"
+#include "ctx_guard.h"
 
 namespace coalibi {
 void set_last_error_detail(const char* msg);
+int check_common(int B, int Hq, int Hkv, int Sq, int Skv, int D, int dtype, int slopes_dtype);
 }
 
 namespace {
@@ -46,9 +53,8 @@ constexpr int kMaxDevices = 64;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
 
 struct NoallocDevice {
-  std::once_flag once;
-  void* ptr = nullptr;
-  cudaError_t err = cudaSuccess;
+  std::mutex mu;
+  void* ptr = nullptr;  // set once, by the first successful lookup on the device
 };
 NoallocDevice g_noalloc[kMaxDevices];
 
@@ -56,7 +62,10 @@ NoallocDevice g_noalloc[kMaxDevices];
 
 extern "C" int coalibi_bwd_noalloc(const CoalibiBwdArgs* args, void* stream) {
   if (args == nullptr || args->q == nullptr) return COALIBI_ERR_NULL_POINTER;
-  // Size check first: pure arithmetic, nothing touches the device.
+  // Shape and size checks first: pure arithmetic, nothing touches the device.
+  if (int rc = coalibi::check_common(args->B, args->Hq, args->Hkv, args->Sq, args->Skv, args->D, args->dtype,
+                                     args->slopes_dtype))
+    return rc;
   const size_t need = coalibi_bwd_workspace_bytes(args->B, args->Hq, args->Hkv, args->Sq, args->Skv, args->D);
   if (need == 0) return COALIBI_ERR_SHAPE;
   if (need > kNoallocScratchBytes) {
@@ -68,31 +77,36 @@ extern "C" int coalibi_bwd_noalloc(const CoalibiBwdArgs* args, void* stream) {
     coalibi::set_last_error_detail(msg);
     return COALIBI_ERR_WORKSPACE;
   }
-  // Make the device that owns q current before touching per-device state.
-  cudaPointerAttributes attr;
-  if (cudaPointerGetAttributes(&attr, args->q) != cudaSuccess || attr.device < 0 || attr.device >= kMaxDevices) {
+  // Per-device state is touched with the device that owns q current; the guard
+  // puts the caller's context back on return.
+  coalibi::CtxGuard guard;
+  if (int rc = coalibi::enter_device(args->q, stream)) return rc;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
     cudaGetLastError();
     return COALIBI_ERR_DEVICE;
   }
-  if (cudaSetDevice(attr.device) != cudaSuccess) {
-    cudaGetLastError();
-    return COALIBI_ERR_DEVICE;
-  }
-  NoallocDevice& st = g_noalloc[attr.device];
-  std::call_once(st.once, [&st] {
-    void* p = nullptr;
-    st.err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    st.ptr = (st.err == cudaSuccess) ? p : nullptr;
-  });
-  if (st.err != cudaSuccess || st.ptr == nullptr) {
-    char msg[160];
-    snprintf(msg, sizeof(msg), "coalibi_bwd_noalloc: cudaGetSymbolAddress failed: %s",
-             cudaGetErrorString(st.err));
-    coalibi::set_last_error_detail(msg);
-    return COALIBI_ERR_LAUNCH;
+  NoallocDevice& st = g_noalloc[dev];
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(st.mu);
+    if (st.ptr == nullptr) {
+      void* p = nullptr;
+      const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+      if (err != cudaSuccess || p == nullptr) {
+        cudaGetLastError();
+        char msg[160];
+        snprintf(msg, sizeof(msg), "coalibi_bwd_noalloc: cudaGetSymbolAddress failed: %s",
+                 cudaGetErrorString(err));
+        coalibi::set_last_error_detail(msg);
+        return COALIBI_ERR_LAUNCH;
+      }
+      st.ptr = p;
+    }
+    scratch = st.ptr;
   }
   CoalibiBwdArgs a = *args;
-  a.workspace = st.ptr;
+  a.workspace = scratch;
   a.workspace_bytes = kNoallocScratchBytes;
   return coalibi_bwd(&a, stream);
 }

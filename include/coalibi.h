@@ -16,7 +16,10 @@
  *
  * The library never allocates device memory, never synchronises and only
  * enqueues work on the stream it is given (a cudaStream_t passed as void*; NULL
- * means the legacy default stream).  Calls are reentrant and thread-safe across
+ * means the legacy default stream), which must belong to the device that holds
+ * the tensors (else COALIBI_ERR_DEVICE).  Each call makes that device current
+ * while it runs and puts the calling thread's previous CUDA context (possibly
+ * none) back before it returns.  Calls are reentrant and thread-safe across
  * streams and devices.  Each function returns COALIBI_OK or an error code;
  * coalibi_strerror() names it.  Kernel-side failures (a bounded wait that timed
  * out) are reported asynchronously through the optional device status word.
@@ -48,7 +51,7 @@ enum coalibi_error {
   COALIBI_ERR_LAUNCH = 6,       /* CUDA launch / attribute error */
   COALIBI_ERR_TENSOR_MAP = 7,   /* cuTensorMapEncodeTiled failed or unavailable */
   COALIBI_ERR_WORKSPACE = 8,    /* workspace missing or smaller than coalibi_bwd_workspace_bytes() */
-  COALIBI_ERR_DEVICE = 9,       /* current device is not sm_100 */
+  COALIBI_ERR_DEVICE = 9,       /* device is not sm_100, or the stream is on another device */
   COALIBI_ERR_TIMEOUT = 10      /* device status only: a bounded wait expired */
 };
 
@@ -149,8 +152,10 @@ int coalibi_bwd_phases(const CoalibiBwdArgs* args, int phase_mask, void* stream)
  * COALIBI_NOALLOC_SCRATCH_BYTES per GPU, held until the process exits; problems
  * needing more (coalibi_bwd_workspace_bytes() > that) return COALIBI_ERR_WORKSPACE
  * without launching.  The first call on each device looks up the array's device
- * address (cudaGetSymbolAddress); make it before any stream capture.  All calls on
- * a device share the array, so calls that overlap on the GPU race: serialise them. */
+ * address (cudaGetSymbolAddress); make it before any stream capture.  The address
+ * is not looked up again, so it is stale after cudaDeviceReset on that device.
+ * All calls on a device share the array, so calls that overlap on the GPU race:
+ * serialise them. */
 int coalibi_bwd_noalloc(const CoalibiBwdArgs* args, void* stream);
 
 /* Self-test of the kernels' bounded waits, with no counterpart in the reference:
@@ -161,6 +166,16 @@ int coalibi_bwd_noalloc(const CoalibiBwdArgs* args, void* stream);
  * 2000) and the CUDA context stays usable.  Returns the launch result; read
  * *status after synchronising the stream. */
 int coalibi_selftest_wait_timeout(unsigned int timeout_ms, int* status, void* stream);
+
+/* The launch configuration this library picks for a problem, as one line of
+ * text: the counterpart of the reference's COALIBI_VERBOSE=1 print of the
+ * configuration its autotuner chose (co_alibi_attn/co_alibi_attn.py:58-63 for the
+ * forward, :125-130 for the backward).  which: 0 forward (coalibi_fwd), 1 decode
+ * forward (coalibi_fwd_decode), 2 backward (coalibi_bwd); device: the CUDA device
+ * index (for its SM count).  Writes a NUL-terminated description into buf,
+ * truncated to buf_len bytes.  Launches nothing and changes no CUDA state. */
+int coalibi_describe_launch(int which, int B, int Hq, int Hkv, int Sq, int Skv, int D, int device,
+                            char* buf, size_t buf_len);
 
 /* Static name of an error code. */
 const char* coalibi_strerror(int code);

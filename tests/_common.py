@@ -80,3 +80,40 @@ def oracle_fwd_pv(q, k, v, causal, sm_scale, bias_max=8.0, compute_dtype=torch.f
     hq, hkv = q.shape[1], k.shape[1]
     va = v.to(compute_dtype).abs().repeat_interleave(hq // hkv, dim=1)
     return o, lse, rs, it["s"] @ va
+
+
+def oracle_slice(q, k, v, do, slopes, b, h, causal, sm_scale=None, rows_per_chunk=2048,
+                 compute_dtype=torch.float32):
+    """The oracle on one (b, h) slice, evaluated in blocks of query rows so that
+    long sequences (S = 8192) stay within a few GB of host memory.  Rows are
+    independent in the forward and in dQ; dK / dV are sums over rows, so the blocks'
+    contributions are added.  Returns (o, lse, rowsig, P@|V|) and, when ``do`` is
+    given, (dq, dk, dv) of this query head (dK / dV before any GQA group sum)."""
+    Hq, Hkv = q.shape[1], k.shape[1]
+    g = h // (Hq // Hkv)
+    ks, vs = k[b:b + 1, g:g + 1], v[b:b + 1, g:g + 1]
+    sl = slopes[h:h + 1]
+    Sq = q.shape[2]
+    outs = {n: [] for n in ("o", "lse", "rs", "pv", "dq")}
+    dk = dv = None
+    va = vs.to(compute_dtype).abs()
+    for r0 in range(0, Sq, rows_per_chunk):
+        r1 = min(Sq, r0 + rows_per_chunk)
+        qs = q[b:b + 1, h:h + 1, r0:r1]
+        o, lse, rs, it = orc.forward(qs, ks, vs, sl, causal, sm_scale, compute_dtype,
+                                     return_intermediates=True, q_offset=r0)
+        outs["o"].append(o[0, 0])
+        outs["lse"].append(lse[0, 0])
+        outs["rs"].append(rs[0, 0])
+        outs["pv"].append((it["s"] @ va)[0, 0])
+        if do is not None:
+            dq_c, dk_c, dv_c = orc.backward(qs, ks, vs, do[b:b + 1, h:h + 1, r0:r1], sl, causal, sm_scale,
+                                            compute_dtype, q_offset=r0, intermediates=it)
+            outs["dq"].append(dq_c[0, 0])
+            dk = dk_c[0, 0] if dk is None else dk + dk_c[0, 0]
+            dv = dv_c[0, 0] if dv is None else dv + dv_c[0, 0]
+        del it
+    fwd = tuple(torch.cat(outs[n]) for n in ("o", "lse", "rs", "pv"))
+    if do is None:
+        return fwd
+    return fwd + (torch.cat(outs["dq"]), dk, dv)

@@ -1,9 +1,10 @@
 """Generate the golden vectors in this folder from the reference's own Python code.
 
-Run once, in a container where the reference checkout is mounted (default
-``/root/reference``; override with ``COALIBI_REFERENCE``)::
+Run once, in a container where a checkout of the reference is available, with
+``COALIBI_REFERENCE`` naming the checkout's root directory (the one holding
+``model.py`` and ``co_alibi_attn/``)::
 
-    python tests/golden/make_golden.py
+    COALIBI_REFERENCE=<path to the reference checkout> python tests/golden/make_golden.py
 
 What is recorded (all float64 unless noted), each from the reference code path
 named beside it:
@@ -33,11 +34,12 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("COALIBI_REFERENCE", "/root/reference")
-
-
 def _load_reference():
-    sys.path.insert(0, REF)
+    ref = os.environ.get("COALIBI_REFERENCE")
+    if not ref or not os.path.isdir(os.path.join(ref, "co_alibi_attn")):
+        raise SystemExit("set COALIBI_REFERENCE to the reference checkout's root directory "
+                         "(the one holding model.py and co_alibi_attn/)")
+    sys.path.insert(0, ref)
     import model  # noqa: E402
     from co_alibi_attn.co_alibi_attn import _get_coalibi_slopes  # noqa: E402
     import co_alibi_attn.benchmark_fwd_pass as bfp  # noqa: E402

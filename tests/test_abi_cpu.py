@@ -76,6 +76,23 @@ def test_bwd_validation_and_phase_mask():
     big.B, big.Hq, big.Hkv, big.Sq, big.Skv, big.D = 8, 16, 16, 4096, 4096, 128
     assert lib.coalibi_bwd_noalloc(ctypes.byref(big), None) == 8  # exceeds the static scratch
     assert "static scratch" in lib.coalibi_last_error().decode()
+    # invalid shapes get the same status as from coalibi_bwd, before the size check
+    bad = _lib.CoalibiBwdArgs(**{f: getattr(big, f) for f, _ in _lib.CoalibiBwdArgs._fields_})
+    bad.Hq, bad.Hkv = 6, 4
+    assert lib.coalibi_bwd_noalloc(ctypes.byref(bad), None) == 4
+    bad.Hq, bad.Hkv, bad.B, bad.Sq = 16, 16, 1 << 20, 1 << 20  # B * Hq * query tiles overflows int32
+    assert lib.coalibi_bwd_noalloc(ctypes.byref(bad), None) == 4
+    bad.B, bad.Sq, bad.D = 1, 128, 96
+    assert lib.coalibi_bwd_noalloc(ctypes.byref(bad), None) == 2
+
+
+def test_describe_launch_validates_before_device_use():
+    from co_alibi_attn import _lib
+    lib = _lib.load()
+    buf = ctypes.create_string_buffer(256)
+    assert lib.coalibi_describe_launch(0, 1, 2, 2, 128, 128, 96, 0, buf, len(buf)) == 2
+    assert lib.coalibi_describe_launch(0, 1, 6, 4, 128, 128, 128, 0, buf, len(buf)) == 4
+    assert lib.coalibi_describe_launch(0, 1, 2, 2, 128, 128, 128, 0, None, 0) == 1
 
 
 def test_slope_table_matches_reference_fixture():

@@ -88,17 +88,19 @@ def test_backward_golden_fixtures(api, path):
 
 
 def test_backward_bench_shape_sampled(api):
-    """README bench shape (B8 H16 S4096 D128 fp16 causal); the oracle checks two
-    (b, h) slices in float32 on the CPU."""
+    """README bench shape (B8 H16 S4096 D128 fp16 causal); the oracle checks eight
+    (b, h) slices in float32 on the CPU, from the first and the last CTAs of the
+    pass A grid (query-major) and the pass B grid (key-major) and between them."""
     from oracle import coalibi_oracle as orc
+    from tests._common import oracle_slice
+    from tests.test_fwd_parity import BENCH_SLICES
     B, H, S, D = 8, 16, 4096, 128
     q, k, v, do = make_inputs(B, H, H, S, S, D, torch.float16, seed=0)
     _, dq, dk, dv = _run(api, q, k, v, do, True, 1.0 / math.sqrt(D))
     sl = orc.api_slopes(H, 8.0, torch.float16)
-    res = orc.forward_sliced(q, k, v, sl, True, None, torch.float32, units=[(0, 0), (5, 11)],
-                             with_backward=True, do=do)
-    for (b, h), t in res.items():
-        for name, x, r in (("dq", dq[b, h], t[3]), ("dk", dk[b, h], t[4]), ("dv", dv[b, h], t[5])):
+    for (b, h) in BENCH_SLICES:
+        t = oracle_slice(q, k, v, do, sl, b, h, True)
+        for name, x, r in (("dq", dq[b, h], t[4]), ("dk", dk[b, h], t[5]), ("dv", dv[b, h], t[6])):
             e = rel_err(x, r)
             assert e <= GRAD_REL, f"(b={b}, h={h}) {name} relative error {e:.3e}"
 

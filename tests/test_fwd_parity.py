@@ -94,41 +94,55 @@ def test_forward_golden_fixtures(api, path):
     assert (o[..., :D0] - o_ref).abs().max().item() < 2e-3
 
 
+# (b, h) slices of the bench shape checked against the oracle.  At B8 H16 S4096 the
+# forward is persistent (4,096 (head, query tile) items over 148 CTAs, 28 rounds,
+# heads taken in groups of 8, longest query tiles first): (0, 0..7) hold the first
+# round's items (query tiles 14-31 of heads 0-7), (7, 8..15) the last round's (query
+# tiles 0-12 of the last group), the others sit in between.  Whole slices are
+# compared, so every query tile of each is covered.
+BENCH_SLICES = [(0, 0), (0, 5), (0, 7), (2, 12), (3, 7), (4, 2), (7, 8), (7, 15)]
+
+
 def test_forward_bench_shape_sampled(api):
     """The README bench shape (B8 H16 S4096 D128 fp16 causal) on the GPU; the oracle
-    checks a sample of (b, h) slices in float32."""
+    checks eight (b, h) slices in float32 (O, lse and row_sig_total)."""
     from oracle import coalibi_oracle as orc
+    from co_alibi_attn.co_alibi_attn import _fwd, _api_slopes
+    from tests._common import oracle_slice
     B, H, S, D = 8, 16, 4096, 128
     q, k, v, _ = make_inputs(B, H, H, S, S, D, torch.float16, seed=0)
-    o = api.co_alibi_attention(q.cuda(), k.cuda(), v.cuda(), causal=True).cpu()
+    qc, kc, vc = q.cuda(), k.cuda(), v.cuda()
+    o = api.co_alibi_attention(qc, kc, vc, causal=True).cpu()
+    _, lse, rs = _fwd(qc, kc, vc, _api_slopes(H, 8.0, torch.float16, qc.device), True, 1.0 / math.sqrt(D))
+    lse, rs = lse.cpu(), rs.cpu()
     sl = orc.api_slopes(H, 8.0, torch.float16)
-    for (b, h) in [(0, 0), (3, 7), (7, 15)]:
-        ref = orc.forward_sliced(q, k, v, sl, True, None, torch.float32, units=[(b, h)])[(b, h)][0]
-        ok, err = check_o(o[b, h], ref, torch.float16)
+    for (b, h) in BENCH_SLICES:
+        o_ref, lse_ref, rs_ref, _ = oracle_slice(q, k, v, None, sl, b, h, True)
+        ok, err = check_o(o[b, h], o_ref, torch.float16)
         assert ok, f"(b={b}, h={h}) O max-abs {err:.3e}"
+        assert (lse[b, h].double() - lse_ref.double()).abs().max().item() < 2e-3, (b, h)
+        assert ((rs[b, h].double() - rs_ref.double()).abs() / rs_ref.double().abs().clamp_min(1.0)).max() < 2e-5
 
 
 @pytest.mark.parametrize("shape", [
-    # B, Hq, Hkv, S, D, causal, dtype: each has at least 12 (head, query tile) items
-    # per SM, so the launch takes the persistent grid
-    (2, 32, 8, 4000, 128, True, torch.bfloat16),    # GQA, ragged last query tile
-    (16, 12, 12, 2048, 64, False, torch.float16),   # D = 64, non-causal
+    # B, Hq, Hkv, S, D, causal, dtype, input std: each has at least 12 (head, query
+    # tile) items per SM, so the launch takes the persistent grid
+    (2, 32, 8, 4000, 128, True, torch.bfloat16, 1.0),    # GQA, ragged last query tile
+    (16, 12, 12, 2048, 64, False, torch.float16, 0.5),   # cfg4: D = 64, non-causal, inputs N(0, 0.5)
 ])
 def test_forward_persistent_grid_sampled(api, shape):
     """The persistent forward on GQA, ragged, bf16, D = 64 and non-causal problems;
-    the oracle checks a sample of (b, h) slices in float32."""
+    the oracle checks a sample of (b, h) slices in float32, the last one in the
+    grid's last round."""
     from oracle import coalibi_oracle as orc
-    B, Hq, Hkv, S, D, causal, dt = shape
-    q, k, v, _ = make_inputs(B, Hq, Hkv, S, S, D, dt, seed=3)
+    from tests._common import oracle_slice
+    B, Hq, Hkv, S, D, causal, dt, std = shape
+    q, k, v, _ = make_inputs(B, Hq, Hkv, S, S, D, dt, seed=3, std=std)
     o = api.co_alibi_attention(q.cuda(), k.cuda(), v.cuda(), causal=causal).cpu()
     sl = orc.api_slopes(Hq, 8.0, dt)
-    G = Hq // Hkv
-    for (b, h) in [(0, 0), (B - 1, Hq // 2 + 1), (B // 2, Hq - 1)]:
-        vs = v[b:b + 1, h // G:h // G + 1]
-        o_ref, _, _, it = orc.forward(q[b:b + 1, h:h + 1], k[b:b + 1, h // G:h // G + 1], vs, sl[h:h + 1],
-                                      causal, None, torch.float32, return_intermediates=True)
-        p_abs_v = (it["s"] @ vs.float().abs())[0, 0]
-        ok, err = check_o(o[b, h], o_ref[0, 0], dt, p_abs_v)
+    for (b, h) in [(0, 0), (B - 1, Hq // 2 + 1), (B // 2, Hq - 1), (B - 1, Hq - 1)]:
+        o_ref, _, _, p_abs_v = oracle_slice(q, k, v, None, sl, b, h, causal)
+        ok, err = check_o(o[b, h], o_ref, dt, p_abs_v)
         assert ok, f"(b={b}, h={h}) O max-abs {err:.3e}"
 
 
