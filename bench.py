@@ -6,13 +6,18 @@
 One step = co_alibi_attention(q, k, v, causal) forward and backward over one
 batch of the named configuration (default cfg2: B=8, H=16, S=4096, D=128, fp16,
 causal -- the reference README's bench shape at the baseline batch).  Inputs are
-seeded synthetic N(0, std) tensors drawn on the CPU and copied to the GPU; all
-of them (512 MiB at cfg2) exceed the 126 MB L2, so no flush is needed between
-steps.  N>1 runs one process per GPU under torchrun; every rank runs its own
-(b, h) units with no collective on the data path ("weak": each rank holds a full
-batch; "strong": the batch's B*Hkv units are split across ranks).  Time is taken
-with CUDA events on the launching stream, between a barrier and a synchronize,
-and the maximum over ranks is reported.
+seeded synthetic N(0, std) tensors drawn on the CPU, one generator per (batch
+element, kv head) unit, and copied to the GPU; all of them (512 MiB at cfg2)
+exceed the 126 MB L2, so no flush is needed between steps.  N>1 runs one process
+per GPU under torchrun; every rank runs its own (b, h) units with no collective
+on the data path ("strong", the default: the config's fixed batch of B*Hkv units
+split into one contiguous block per rank; "weak": every rank holds a full batch).
+Time is taken with CUDA events on the launching stream, between a barrier and a
+synchronize, and the maximum over ranks is reported.  After timing, NCCL gathers
+every rank's outputs for verification (against a single-GPU run of the whole
+batch on rank 0 and against the CPU oracle on sampled slices).  At N=1 the
+reference's own Triton kernels (baseline/triton_ref.py) are timed on the same
+inputs in a subprocess.
 
 ``--config cfg5`` instead times one data-parallel training step of the small
 Co-ALiBi GPT (co_alibi_gpt: 12 layers, d_model 768, 12 heads of D=64, seq 1024,
@@ -56,6 +61,35 @@ NCU_TRAFFIC_CFG2 = {"fwd": 4 * 116.0e6, "bwd_a": 4 * 206.0e6, "bwd_b": 4 * 253.4
 
 def visible(S, causal):
     return S * (S + 1) // 2 if causal else S * S
+
+
+def unit_inputs(cfg, b, g, seed=1000):
+    """Inputs of one (batch element b, kv head g) unit -- K and V of the kv head, Q
+    and dO of its G query heads -- from a CPU generator seeded by the unit's index,
+    so every rank draws exactly its own units of one global batch (and
+    baseline/triton_ref.py the same batch)."""
+    B, Hq, Hkv, S, D, dtype, causal, std, fwd_only = cfg
+    G = Hq // Hkv
+    gen = torch.Generator().manual_seed(seed + b * Hkv + g)
+    q = (torch.randn(G, S, D, generator=gen) * std).to(dtype)
+    k = (torch.randn(1, S, D, generator=gen) * std).to(dtype)
+    v = (torch.randn(1, S, D, generator=gen) * std).to(dtype)
+    do = torch.randn(G, S, D, generator=gen).to(dtype)
+    return q, k, v, do
+
+
+def shard_inputs(cfg, b0, b1, g0, g1, pin=False):
+    """(q, k, v, do) host tensors of units b0 <= b < b1, g0 <= g < g1."""
+    B, Hq, Hkv, S, D, dtype, causal, std, fwd_only = cfg
+    G = Hq // Hkv
+    mk = lambda h: torch.empty(b1 - b0, h, S, D, dtype=dtype, pin_memory=pin)  # noqa: E731
+    q, k, v, do = mk((g1 - g0) * G), mk(g1 - g0), mk(g1 - g0), mk((g1 - g0) * G)
+    for b in range(b0, b1):
+        for g in range(g0, g1):
+            uq, uk, uv, udo = unit_inputs(cfg, b, g)
+            i, j = b - b0, g - g0
+            q[i, j * G:(j + 1) * G], k[i, j], v[i, j], do[i, j * G:(j + 1) * G] = uq, uk[0], uv[0], udo
+    return q, k, v, do
 
 
 def load_peaks():
@@ -269,6 +303,164 @@ def pcie_copy_floor_ms(ins_h, outs_h, dev, reps=3):
         best = min(best, e0.elapsed_time(e1))
     del ins_d, outs_d
     return best
+
+
+def verify_shards(cfg, shard, world, rank, dev, qd, kd, vd, dod, attn, oracle_slices=2):
+    """Verification of the (b, h)-sharded run, outside the timed region: every rank
+    runs its shard once more, NCCL all-gathers the shards' o / dq / dk / dv (the only
+    use of a collective on data), and rank 0 compares the gathered batch with a
+    single-GPU run of the whole batch (at N > 1) and with the CPU oracle on
+    `oracle_slices` (b, h) slices of the first and last ranks' shards.  Returns the
+    summary on rank 0, None elsewhere."""
+    import torch.distributed as dist
+    import co_alibi_attn
+    B, Hq, Hkv, S, D, dtype, causal, std, fwd_only = cfg
+    G = Hq // Hkv
+    qg = qd.detach().clone().requires_grad_(not fwd_only)
+    kg = kd.detach().clone().requires_grad_(not fwd_only)
+    vg = vd.detach().clone().requires_grad_(not fwd_only)
+    if fwd_only:
+        with torch.no_grad():
+            outs = [attn(qg, kg, vg)]
+    else:
+        o = attn(qg, kg, vg)
+        o.backward(dod)
+        outs = [o.detach(), qg.grad, kg.grad, vg.grad]
+    torch.cuda.synchronize()
+    names = ["o", "dq", "dk", "dv"][:len(outs)]
+    # gather: every rank's shard of each output, in rank order (equal sizes by construction)
+    gathered = []
+    for t in outs:
+        t = t.contiguous()
+        if world > 1:
+            buf = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=dev)
+            dist.all_gather_into_tensor(buf, t)
+        else:
+            buf = t.unsqueeze(0)
+        gathered.append(buf)
+    torch.cuda.synchronize()
+    if rank != 0:
+        return None
+    from co_alibi_attn.sharding import shard_plan
+    plans = [shard_plan(B, Hq, Hkv, world, r) if world > 1 else shard for r in range(world)]
+
+    def assemble(i):
+        """The whole batch's output i from the gathered shards (host)."""
+        heads = Hq if names[i] in ("o", "dq") else Hkv
+        per = G if heads == Hq else 1
+        full = torch.empty(B, heads, S, D, dtype=dtype)
+        for r, sh in enumerate(plans):
+            full[sh.b0:sh.b1, sh.g0 * per:sh.g1 * per] = gathered[i][r].cpu()
+        return full
+
+    full = [assemble(i) for i in range(len(names))]
+    out = {"collective": f"NCCL all_gather_into_tensor of each rank's {'/'.join(names)} shard" if world > 1
+           else "none (one rank)", "ranks": world}
+    if world > 1:
+        # rank 0 alone runs the whole batch through the public API and compares
+        q1, k1, v1, do1 = (t.to(dev) for t in shard_inputs(cfg, 0, B, 0, Hkv))
+        q1.requires_grad_(not fwd_only), k1.requires_grad_(not fwd_only), v1.requires_grad_(not fwd_only)
+        if fwd_only:
+            with torch.no_grad():
+                ref = [co_alibi_attn.co_alibi_attention(q1, k1, v1, causal=causal)]
+        else:
+            o1 = co_alibi_attn.co_alibi_attention(q1, k1, v1, causal=causal)
+            o1.backward(do1)
+            ref = [o1.detach(), q1.grad, k1.grad, v1.grad]
+        torch.cuda.synchronize()
+        cmp = {}
+        for n, a, r in zip(names, full, ref):
+            r = r.cpu()
+            cmp[n] = {"bitwise_equal": bool(torch.equal(a, r)),
+                      "max_abs_diff": float((a.float() - r.float()).abs().max())}
+        out["vs_single_gpu_whole_batch"] = cmp
+        del q1, k1, v1, do1, ref
+    # the CPU oracle on sampled slices (first unit of rank 0, last unit of the last rank)
+    sys.path.insert(0, ROOT)
+    from oracle import coalibi_oracle as orc
+    torch.set_num_threads(os.cpu_count() or 1)
+    sl = orc.api_slopes(Hq, 8.0, dtype)
+    picks = [(0, 0), (B - 1, Hq - 1)][:oracle_slices]
+    res = []
+    for (b, h) in picks:
+        g = h // G
+        uq, uk, uv, udo = unit_inputs(cfg, b, g)
+        qs, ks, vs, dos = uq[h - g * G][None, None], uk[None], uv[None], udo[h - g * G][None, None]
+        r = {"b": b, "h": h}
+        if fwd_only:
+            o_r, _, _ = orc.forward(qs, ks, vs, sl[h:h + 1], causal, None, torch.float32)
+        else:
+            o_r, _, _, dq_r, dk_r, dv_r = orc.forward_backward(qs, ks, vs, dos, sl[h:h + 1], causal, None,
+                                                               torch.float32)
+        r["o_max_abs"] = float((full[0][b, h].double() - o_r[0, 0].double()).abs().max())
+        if not fwd_only:
+            rel = lambda x, y: float((x.double() - y.double()).norm() / y.double().norm())  # noqa: E731
+            r["dq_rel"] = rel(full[1][b, h], dq_r[0, 0])
+            if G == 1:  # dk / dv of one query head equal the kv head's only when no group sum is needed
+                r["dk_rel"] = rel(full[2][b, g], dk_r[0, 0])
+                r["dv_rel"] = rel(full[3][b, g], dv_r[0, 0])
+        res.append(r)
+    o_tol = 2e-3 if dtype == torch.float16 else 2e-2
+    ok = all(r["o_max_abs"] <= o_tol and all(r.get(n, 0.0) <= 1e-2 for n in ("dq_rel", "dk_rel", "dv_rel"))
+             for r in res)
+    out["vs_oracle"] = {"slices": res, "o_tol": o_tol, "grad_rel_tol": 1e-2, "pass": ok,
+                        "oracle": "fp32 CPU restatement of model.py (oracle/), one (b, h) slice each"}
+    out["pass"] = ok and all(c["bitwise_equal"] or c["max_abs_diff"] == 0.0
+                             for c in out.get("vs_single_gpu_whole_batch", {}).values())
+    return out
+
+
+def reference_triton_side_by_side(args, cfg, o_ours, ms_ours, fwd_ms_ours, timeout_s=900):
+    """The reference's own Triton kernels on the same inputs and GPU, run by
+    baseline/triton_ref.py in a subprocess (both packages are named co_alibi_attn).
+    Returns its timings, this build's speed-up over them, and the largest
+    difference between its O and this build's on two (b, h) slices."""
+    import tempfile
+    B, Hq, Hkv, S, D, dtype, causal, std, fwd_only = cfg
+    script = os.path.join(ROOT, "baseline", "triton_ref.py")
+    if not os.path.isdir(os.path.join(ROOT, "baseline", "_ref", "co_alibi_attn")):
+        return {"unavailable": "baseline/_ref holds no reference package (python baseline/install_ref.py "
+                               "<reference checkout> installs it)"}
+    with tempfile.TemporaryDirectory() as td:
+        out = os.path.join(td, "ref.json")
+        cmd = [sys.executable, script, "--config", args.config, "--steps", str(max(3, min(args.steps, 10))),
+               "--warmup", "3", "--out", out]
+        if args.batch:
+            cmd += ["--batch", str(args.batch)]
+        env = dict(os.environ)
+        env.pop("COALIBI_VERBOSE", None)
+        try:
+            r = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout_s, env=env)
+        except subprocess.TimeoutExpired:
+            return {"unavailable": f"baseline/triton_ref.py did not finish within {timeout_s} s"}
+        if r.returncode != 0 or not os.path.exists(out):
+            tail = (r.stderr.strip().splitlines() or ["(no output)"])[-1]
+            return {"unavailable": f"baseline/triton_ref.py exited {r.returncode}: {tail}"[:300]}
+        with open(out) as f:
+            ref = json.load(f)
+    E = visible(S, causal) * B * Hq
+    res = {k: ref[k] for k in ("impl", "triton", "first_calls_s", "peak_mem_gb") if k in ref}
+    res["fwd_ms"] = round(ref["fwd_ms"], 4)
+    res["fwd_tflops"] = round(4.0 * D * E / (ref["fwd_ms"] * 1e-3) / 1e12, 2)
+    if fwd_ms_ours:
+        res["fwd_speedup_of_this_build"] = round(ref["fwd_ms"] / fwd_ms_ours, 2)
+    if "bwd_ms" in ref:
+        res["bwd_ms"] = round(ref["bwd_ms"], 4)
+        res["bwd_tflops"] = round(10.0 * D * E / (ref["bwd_ms"] * 1e-3) / 1e12, 2)
+        res["bwd_note"] = "backward(retain_graph=True) replayed on one graph, gradients zeroed each time " \
+                          "(the reference benchmark's convention, co_alibi_attn/benchmark_flops.py:66-92)"
+    if "fwd_bwd_ms" in ref:
+        res["fwd_bwd_ms"] = round(ref["fwd_bwd_ms"], 4)
+        res["fwd_bwd_tflops"] = round(14.0 * D * E / (ref["fwd_bwd_ms"] * 1e-3) / 1e12, 2)
+        res["fwd_bwd_speedup_of_this_build"] = round(ref["fwd_bwd_ms"] / ms_ours, 2)
+    diffs = []
+    for s_ in ref.get("slices", []):
+        o_ref = torch.tensor(s_["o"])
+        diffs.append({"b": s_["b"], "h": s_["h"],
+                      "o_max_abs_diff_vs_this_build": float((o_ours[s_["b"], s_["h"]].float() - o_ref).abs().max())})
+    res["o_compare"] = diffs
+    res["tflops_note"] = "algorithmic causal FLOPs (4 D forward, 10 D backward per visible score), as for this build"
+    return res
 
 
 def run_reference_arm(args, cfg, rank):
@@ -691,13 +883,15 @@ def metric_name(config):
 
 def config_dict(args, cfg):
     B, Hq, Hkv, S, D, dtype, causal, std, fwd_only = cfg
-    per_rank_B = B if args.scaling == "weak" else max(1, B // args.gpus)
+    units_per_rank = B * Hkv if args.scaling == "weak" else B * Hkv // max(1, args.gpus)
     return {"workload": f"{args.config}: co_alibi_attention {'fwd' if fwd_only else 'fwd+bwd'} B={B} Hq={Hq} "
                         f"Hkv={Hkv} S={S} D={D} {str(dtype).split('.')[-1]} "
                         f"{'causal' if causal else 'non-causal'}",
             "global_batch": B * (args.gpus if args.scaling == "weak" else 1), "seq_len": S,
-            "heads": Hq, "kv_heads": Hkv, "head_dim": D, "per_rank_batch": per_rank_B,
-            "parallelism": f"(b,h)-shards x{args.gpus}, no data-path collective",
+            "heads": Hq, "kv_heads": Hkv, "head_dim": D, "units_per_rank": units_per_rank,
+            "parallelism": (f"(b,h)-shards x{args.gpus} ({args.scaling} scaling: "
+                            + ("the fixed batch split over the ranks" if args.scaling == "strong"
+                               else "a full batch per rank") + "), no data-path collective"),
             "l2": "inputs (4 x B*H*S*D*2 bytes) exceed the 126 MB L2; no flush needed"}
 
 
@@ -711,7 +905,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS) + ["cfg5", "decode", "cp"])
-    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
+    ap.add_argument("--scaling", default="strong", choices=["weak", "strong"],
+                    help="strong (default): the config's batch split over the ranks; weak: a full batch per rank")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--batch", type=int, default=None,
                     help="override the config's batch size (small cases for ncu captures)")
@@ -719,7 +914,9 @@ def main():
                     help="--config cp only: override the sequence length (small cases for ncu captures)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-side-by-side", action="store_true",
-                    help="skip the FlashAttention-2 comparison on the same shape (N=1 only)")
+                    help="skip the FlashAttention-2 and reference-Triton comparisons on the same shape (N=1 only)")
+    ap.add_argument("--no-verify", action="store_true",
+                    help="skip the post-timing verification gather (small ncu capture cases)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.config in ("cfg5", "decode", "cp"):
@@ -789,11 +986,8 @@ def main():
             return sharded_attention(q_, k_, v_, shard, Hq, causal=causal)
         return co_alibi_attention(q_, k_, v_, causal=causal)
 
-    g = torch.Generator().manual_seed(1000 + rank)
-    q_h = (torch.randn(B_r, Hq_r, S, D, generator=g) * std).to(dtype).pin_memory()
-    k_h = (torch.randn(B_r, Hkv_r, S, D, generator=g) * std).to(dtype).pin_memory()
-    v_h = (torch.randn(B_r, Hkv_r, S, D, generator=g) * std).to(dtype).pin_memory()
-    do_h = torch.randn(B_r, Hq_r, S, D, generator=g).to(dtype).pin_memory()
+    # weak scaling: every rank holds the whole batch (the same units); strong: its block
+    q_h, k_h, v_h, do_h = shard_inputs(cfg, shard.b0, shard.b1, shard.g0, shard.g1, pin=True)
     q = q_h.to(dev).requires_grad_(not fwd_only)
     k = k_h.to(dev).requires_grad_(not fwd_only)
     v = v_h.to(dev).requires_grad_(not fwd_only)
@@ -906,14 +1100,23 @@ def main():
         kernels[name] = d
     roof = {"bound": "tensor", "kernel": dom, "achieved": round(ach, 2), "peak": burst, "unit": "TFLOP/s",
             "frac": round(ach / burst, 4), "peak_source": f"{peak_src} bf16_tflops (burst)",
-            "traffic": NCU_TRAFFIC_CFG2.get(dom) if args.config == "cfg2" and args.scaling == "weak" else None,
+            "traffic": NCU_TRAFFIC_CFG2.get(dom) if args.config == "cfg2" and B_r * Hkv_r == 8 * 16 else None,
             "flops_per_launch": per_kernel_flops[dom],
             "note": "algorithmic FLOPs on causal-visible scores of the kernel's GEMMs "
                     "(fwd 4D, pass A 6D, pass B 8D per score) / mean CUDA-event duration in the timed region; "
                     "second roofline: mufu_frac = MUFU ops per score (tanh + ex2 = 2, 1.75 where a quarter of the ex2 is a polynomial) / (16 ops/clk/SM x 148 SMs x sampled clock)"}
 
-    side = None
+    verification = None
+    if not args.no_verify:
+        verification = verify_shards(cfg, shard, world, rank, dev, q, k, v, do, attn)
+
+    side = ref_triton = None
     if world == 1 and not args.no_side_by_side:
+        with torch.no_grad():
+            o_ours = co_alibi_attention(q, k, v, causal=causal).cpu()
+        torch.cuda.synchronize()
+        ref_triton = reference_triton_side_by_side(args, cfg, o_ours, ms_max, fwd_ms)
+        del o_ours
         side = flash_side_by_side(cfg, dev, max(3, min(args.steps, 50)), args.warmup)
 
     cpu = None
@@ -944,6 +1147,8 @@ def main():
                     "note": "copy_only_ms: the same bytes copied host->device and device->host at once (pinned "
                             "buffers, two streams, no kernels); e2e can be no faster"},
             "gpu_launches": kernels_per_step * args.steps, "clocks": clocks, "device_status": status,
+            "verification": verification,
+            "reference_triton": ref_triton,
             "side_by_side": side,
         }
         print(json.dumps(line), flush=True)

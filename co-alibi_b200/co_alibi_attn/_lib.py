@@ -40,8 +40,9 @@ class CoalibiBwdArgs(ctypes.Structure):
 
 
 EXPORTS = ("coalibi_fwd", "coalibi_fwd_decode", "coalibi_fwd_decode_workspace_bytes", "coalibi_bwd",
-           "coalibi_bwd_carry", "coalibi_bwd_phases", "coalibi_bwd_noalloc",
-           "coalibi_bwd_workspace_bytes", "coalibi_selftest_wait_timeout", "coalibi_strerror",
+           "coalibi_bwd_carry", "coalibi_bwd_phases", "coalibi_bwd_noalloc", "coalibi_bwd_workspace_size",
+           "coalibi_bwd_workspace_bytes", "coalibi_bwd_workspace_min_bytes", "coalibi_selftest_wait_timeout",
+           "coalibi_strerror",
            "coalibi_abi_version", "coalibi_last_error", "coalibi_describe_launch")
 
 NOALLOC_SCRATCH_BYTES = 64 << 20  # COALIBI_NOALLOC_SCRATCH_BYTES
@@ -78,13 +79,17 @@ def load():
             lib.coalibi_bwd_noalloc.restype = c_int
             lib.coalibi_bwd_workspace_bytes.argtypes = [c_int] * 6
             lib.coalibi_bwd_workspace_bytes.restype = c_size_t
+            lib.coalibi_bwd_workspace_min_bytes.argtypes = [c_int] * 6
+            lib.coalibi_bwd_workspace_min_bytes.restype = c_size_t
+            lib.coalibi_bwd_workspace_size.argtypes = [ctypes.POINTER(CoalibiBwdArgs)]
+            lib.coalibi_bwd_workspace_size.restype = c_size_t
             lib.coalibi_selftest_wait_timeout.argtypes = [ctypes.c_uint, c_void_p, c_void_p]
             lib.coalibi_selftest_wait_timeout.restype = c_int
             lib.coalibi_strerror.argtypes = [c_int]
             lib.coalibi_strerror.restype = ctypes.c_char_p
             lib.coalibi_last_error.argtypes = []
             lib.coalibi_last_error.restype = ctypes.c_char_p
-            lib.coalibi_describe_launch.argtypes = [c_int] * 8 + [ctypes.c_char_p, c_size_t]
+            lib.coalibi_describe_launch.argtypes = [c_int] * 9 + [ctypes.c_char_p, c_size_t]
             lib.coalibi_describe_launch.restype = c_int
             lib.coalibi_abi_version.argtypes = []
             lib.coalibi_abi_version.restype = c_int
@@ -95,10 +100,11 @@ def load():
 FWD, DECODE, BWD = 0, 1, 2  # `which` of coalibi_describe_launch
 
 
-def describe_launch(which: int, B: int, Hq: int, Hkv: int, Sq: int, Skv: int, D: int, device: int) -> str:
+def describe_launch(which: int, B: int, Hq: int, Hkv: int, Sq: int, Skv: int, D: int, causal: bool,
+                    device: int) -> str:
     """The library's launch configuration for a problem, as text (coalibi_describe_launch)."""
-    buf = ctypes.create_string_buffer(512)
-    check(load().coalibi_describe_launch(which, B, Hq, Hkv, Sq, Skv, D, device, buf, len(buf)),
+    buf = ctypes.create_string_buffer(768)
+    check(load().coalibi_describe_launch(which, B, Hq, Hkv, Sq, Skv, D, 1 if causal else 0, device, buf, len(buf)),
           "coalibi_describe_launch")
     return buf.value.decode()
 

@@ -101,12 +101,12 @@ def _check_inputs(q, k, v, slopes):
         raise TypeError(f"co_alibi_attn: slopes must be float16/bfloat16/float32, got {slopes.dtype}")
 
 
-def _verbose(which, B, Hq, Hkv, Sq, Skv, D, device):
+def _verbose(which, B, Hq, Hkv, Sq, Skv, D, causal, device):
     """With COALIBI_VERBOSE=1, print the launch configuration of each call, as the
     reference prints its autotuned configs (co_alibi_attn/co_alibi_attn.py:58-63,
     :125-130)."""
     if os.getenv("COALIBI_VERBOSE", "0") == "1":
-        print(f"[Co-ALIBI] {_lib.describe_launch(which, B, Hq, Hkv, Sq, Skv, D, device.index)}")
+        print(f"[Co-ALIBI] {_lib.describe_launch(which, B, Hq, Hkv, Sq, Skv, D, causal, device.index)}")
 
 
 # Sq limit of coalibi_fwd_decode (COALIBI_DECODE_MAX_SQ in coalibi.h)
@@ -147,31 +147,35 @@ def _fwd(q, k, v, slopes, causal, sm_scale, decode=None):
     if rec is not None:
         e1.record()
         rec.setdefault("fwd", []).append((e0, e1))
-    _verbose(_lib.DECODE if decode else _lib.FWD, B, Hq, Hkv, Sq, Skv, D, q.device)
+    _verbose(_lib.DECODE if decode else _lib.FWD, B, Hq, Hkv, Sq, Skv, D, causal, q.device)
     return o, lse, rowsig
 
 
-def _bwd(q, k, v, o, do, lse, rowsig, slopes, causal, sm_scale, dA_carry_in=None):
+def _bwd(q, k, v, o, do, lse, rowsig, slopes, causal, sm_scale, dA_carry_in=None, min_workspace=False):
     """Backward kernels.  ``dA_carry_in`` (float32 [B, Hq, Sq]) marks k / v as one
     key shard of longer rows (coalibi_bwd_carry): the sum of P (dP - delta) over the
     keys left of the shard; o, lse and do are then the whole row's, rowsig the
-    sigmoid total of the shard and of every key right of it."""
+    sigmoid total of the shard and of every key right of it.  The workspace is the
+    library's preferred size for the problem (coalibi_bwd_workspace_size: P / dS
+    stored by the first kernel while that stays below 24 GiB); ``min_workspace``
+    gives it the smallest size instead, which makes the backward recompute P / dS."""
     B, Hq, Sq, D = q.shape
     Hkv, Skv = k.shape[1], k.shape[2]
     lib = _lib.load()
     dq = torch.empty_like(q)
     dk = torch.empty_like(k)
     dv = torch.empty_like(v)
-    nbytes = lib.coalibi_bwd_workspace_bytes(B, Hq, Hkv, Sq, Skv, D)
-    ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
     a = _lib.CoalibiBwdArgs(
         q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), o=o.data_ptr(), dout=do.data_ptr(),
         lse=lse.data_ptr(), rowsig=rowsig.data_ptr(), slopes=slopes.data_ptr(),
-        dq=dq.data_ptr(), dk=dk.data_ptr(), dv=dv.data_ptr(),
-        workspace=ws.data_ptr(), workspace_bytes=nbytes,
+        dq=dq.data_ptr(), dk=dk.data_ptr(), dv=dv.data_ptr(), workspace=None, workspace_bytes=0,
         B=B, Hq=Hq, Hkv=Hkv, Sq=Sq, Skv=Skv, D=D, dtype=_DTYPES[q.dtype],
         slopes_dtype=_SLOPE_DTYPES[slopes.dtype], causal=1 if causal else 0, sm_scale=float(sm_scale),
         status=_status_word(q.device).data_ptr(), timeout_ms=0)
+    nbytes = (lib.coalibi_bwd_workspace_min_bytes(B, Hq, Hkv, Sq, Skv, D) if min_workspace
+              else lib.coalibi_bwd_workspace_size(a))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), nbytes
     stream = torch.cuda.current_stream(q.device).cuda_stream
     rec = kernel_events
     if dA_carry_in is not None:
@@ -191,7 +195,7 @@ def _bwd(q, k, v, o, do, lse, rowsig, slopes, causal, sm_scale, dA_carry_in=None
             _lib.check(lib.coalibi_bwd_phases(a, bit, stream), "coalibi_bwd_phases")
             e1.record()
             rec.setdefault(name, []).append((e0, e1))
-    _verbose(_lib.BWD, B, Hq, Hkv, Sq, Skv, D, q.device)
+    _verbose(_lib.BWD, B, Hq, Hkv, Sq, Skv, D, causal, q.device)
     return dq, dk, dv
 
 

@@ -36,21 +36,81 @@
 
 namespace coalibi {
 
+// Two ways to run passes A and B, chosen per call by the workspace it gets:
+//  * stored (preferred while its scratch stays under kStoredCapBytes): pass A
+//    also writes P and dS -- the 16-bit values its own dQ MMA consumes -- as
+//    128 x 128 tiles, one per visible (query tile, key tile) pair, and pass B is
+//    a streaming GEMM (dV = P^T dO, dK = dS^T Q) with no per-score maths;
+//  * recompute (bounded scratch, O(S^2 / 32)): pass A records the running sums
+//    (z suffix, c prefix) every 32 keys and pass B recomputes S, dP, P and dS.
 struct BwdWorkspace {
-  size_t delta_off, carry_off, total;
+  size_t delta_off, carry_off, p_off, ds_off, total;
+  long long tiles_per_head;  // stored: visible tiles per (b, q head)
+  bool stored;
 };
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// delta: float [B*Hq][sq_pad];  carry: float2 [B*Hq][n_kb32][sq_pad] (one pair per 32 keys)
-inline BwdWorkspace bwd_workspace_layout(int B, int Hq, int Sq, int Skv) {
+// P / dS scratch of the stored path is used only while it stays below this size;
+// larger problems recompute in pass B (their scratch grows as S^2 / 32 instead).
+constexpr size_t kStoredCapBytes = (size_t)24 << 30;
+constexpr size_t kTileBytes = 128 * 128 * 2;  // one 16-bit [128 rows][128 keys] tile
+
+// Visible key tiles of query tile qt: top-left causal key tile kt is seen iff kt <= qt.
+__host__ __device__ inline int tiles_in_row(int qt, int n_kv, bool causal) {
+  return causal ? min(qt + 1, n_kv) : n_kv;
+}
+// Index of tile (qt, 0) among a head's visible tiles, rows in order.
+__host__ __device__ inline long long tile_row_start(int qt, int n_kv, bool causal) {
+  if (!causal) return (long long)qt * n_kv;
+  if (qt <= n_kv) return (long long)qt * (qt + 1) / 2;
+  return (long long)n_kv * (n_kv + 1) / 2 + (long long)(qt - n_kv) * n_kv;
+}
+
+// recompute: delta float [B*Hq][sq_pad]; carry float2 [B*Hq][n_kb32][sq_pad] (one pair per 32 keys)
+inline BwdWorkspace bwd_workspace_recompute(int B, int Hq, int Sq, int Skv) {
   const size_t sq_pad = (size_t)((Sq + 127) / 128) * 128;
   const size_t nkb = (size_t)((Skv + 31) / 32);
-  BwdWorkspace w;
+  BwdWorkspace w{};
+  w.stored = false;
   w.delta_off = 0;
   w.carry_off = align256((size_t)B * Hq * sq_pad * 4);
   w.total = w.carry_off + align256((size_t)B * Hq * nkb * sq_pad * 8);
   return w;
+}
+
+// stored: delta float [B*Hq][sq_pad]; P, dS 16-bit [B*Hq][tiles_per_head][16][128][8]: each tile
+// in 8-key segments of all 128 rows (the no-swizzle core-matrix order the MMA reads)
+inline BwdWorkspace bwd_workspace_stored(int B, int Hq, int Sq, int Skv, bool causal) {
+  const int n_q = (Sq + 127) / 128, n_kv = (Skv + 127) / 128;
+  const size_t sq_pad = (size_t)n_q * 128;
+  BwdWorkspace w{};
+  w.stored = true;
+  w.tiles_per_head = tile_row_start(n_q, n_kv, causal);
+  const size_t pbytes = (size_t)B * Hq * (size_t)w.tiles_per_head * kTileBytes;
+  w.delta_off = 0;
+  w.p_off = align256((size_t)B * Hq * sq_pad * 4);
+  w.ds_off = w.p_off + pbytes;
+  w.total = w.ds_off + pbytes;
+  return w;
+}
+
+// The layout a call uses: stored when the caller's workspace holds it, else
+// recompute; total == 0 when neither fits.
+inline BwdWorkspace bwd_workspace_for(int B, int Hq, int Sq, int Skv, bool causal, size_t provided) {
+  const BwdWorkspace s = bwd_workspace_stored(B, Hq, Sq, Skv, causal);
+  if (provided >= s.total) return s;
+  BwdWorkspace r = bwd_workspace_recompute(B, Hq, Sq, Skv);
+  if (provided < r.total) r.total = 0;
+  return r;
+}
+
+// The size to allocate: the stored layout while its P / dS scratch is below the
+// cap, else the recompute layout.
+inline size_t bwd_workspace_preferred(int B, int Hq, int Sq, int Skv, bool causal) {
+  const BwdWorkspace s = bwd_workspace_stored(B, Hq, Sq, Skv, causal);
+  if (s.total - s.p_off <= kStoredCapBytes) return s.total;
+  return bwd_workspace_recompute(B, Hq, Sq, Skv).total;
 }
 
 struct BwdParams {
@@ -63,7 +123,10 @@ struct BwdParams {
   void* dk;
   void* dv;
   float* delta;
-  float2* carry;
+  float2* carry;     // recompute path: pass A -> pass B running sums (null on the stored path)
+  uint16_t* pstore;  // stored path: P tiles [B*Hq][tiles_per_head][16][128][8] (null on the recompute path)
+  uint16_t* dsstore; // stored path: dS tiles, same layout
+  long long tiles_per_head;
   int B, Hq, Hkv, Sq, Skv;
   int slopes_dtype;
   int causal;
@@ -234,10 +297,10 @@ __device__ __forceinline__ float bwd_a_sig(uint32_t* sreg, float* sg, int key0, 
 }
 
 // Phase 2 on 16 keys: P from the sigmoid suffix zz, dA = P (dP - delta) over the
-// xa registers; returns the sum of dA.
-template <bool MASK>
+// xa registers; returns the sum of dA.  With STORE, also P packed to 16 bits in pk.
+template <bool MASK, bool BF16, bool STORE>
 __device__ __forceinline__ float bwd_a_da(uint32_t* xa, const float* sg, const uint32_t* dpr, int key0, int lim,
-                                          float slope2, float delta, float& zz) {
+                                          float slope2, float delta, float& zz, uint32_t* pk) {
   float2 tot = make_float2(0.f, 0.f);
 #pragma unroll
   for (int j = 0; j < 16; j += 2) {
@@ -253,6 +316,7 @@ __device__ __forceinline__ float bwd_a_da(uint32_t* xa, const float* sg, const u
     P.y = ex2_approx(e.y);
     if (MASK && key0 + j >= lim) P.x = 0.f;
     if (MASK && key0 + j + 1 >= lim) P.y = 0.f;
+    if (STORE) pk[j / 2] = pack2<BF16>(P.x, P.y);
     const float2 dA = __fmul2_rn(
         P, __fadd2_rn(make_float2(__uint_as_float(dpr[j]), __uint_as_float(dpr[j + 1])), make_float2(-delta, -delta)));
     xa[j] = __float_as_uint(dA.x);
@@ -262,7 +326,7 @@ __device__ __forceinline__ float bwd_a_da(uint32_t* xa, const float* sg, const u
   return tot.x + tot.y;
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool STORE>
 __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
     coalibi_bwd_a_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
                          const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
@@ -484,7 +548,13 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
     const float delta = p.delta[(size_t)bh * p.sq_pad + row];
     const int lim = row_ok ? (p.causal ? min(row + 1, p.Skv) : p.Skv) : 0;
     const bool rows_partial = (qt * L::BM + L::BM > p.Sq);
-    float2* carry_row = p.carry + (size_t)bh * p.n_kb32 * p.sq_pad + row;
+    float2* carry_row = STORE ? nullptr : p.carry + (size_t)bh * p.n_kb32 * p.sq_pad + row;
+    // stored path: row t_row of the (qt, n) P / dS tiles; a tile holds 16 segments of
+    // 8 keys x 128 rows, so this thread's 32 keys are segments 4 wg .. 4 wg + 3 and a
+    // warp (32 consecutive rows) writes 512 contiguous bytes per segment
+    const size_t tile0 = STORE ? ((size_t)bh * p.tiles_per_head + tile_row_start(qt, p.n_kvtiles, p.causal != 0)) *
+                                     (size_t)(128 * 128) + (size_t)(4 * wg * 128 + t_row) * 8
+                               : 0;
     bool ok = true;
     for (int n = 0; n < N; ++n) {
       const int key0 = n * BN + 32 * wg;  // first key of this thread's chunk
@@ -533,8 +603,16 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(dp_free);
           }
-          dtot += masked ? bwd_a_da<true>(xa + 16 * hh, sg + 16 * hh, dpr, key0 + 16 * hh, lim, slope2, delta, zz)
-                         : bwd_a_da<false>(xa + 16 * hh, sg + 16 * hh, dpr, key0 + 16 * hh, lim, slope2, delta, zz);
+          uint32_t pk[8];
+          dtot += masked ? bwd_a_da<true, BF16, STORE>(xa + 16 * hh, sg + 16 * hh, dpr, key0 + 16 * hh, lim, slope2,
+                                                       delta, zz, pk)
+                         : bwd_a_da<false, BF16, STORE>(xa + 16 * hh, sg + 16 * hh, dpr, key0 + 16 * hh, lim, slope2,
+                                                        delta, zz, pk);
+          if (STORE) {
+            uint16_t* dst = p.pstore + tile0 + (size_t)n * (128 * 128) + (2 * hh) * 1024;
+            *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            *reinterpret_cast<uint4*>(dst + 1024) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          }
         }
       }
       // dA prefix sum before this chunk's first key, handed along the same way (the
@@ -551,7 +629,7 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
         mbar_arrive(&clink[quarter * L::NWG + nwg]);
       }
       const int kb32 = key0 / 32;
-      if (kb32 < p.n_kb32) carry_row[(size_t)kb32 * p.sq_pad] = make_float2(z0, cc);
+      if (!STORE && kb32 < p.n_kb32) carry_row[(size_t)kb32 * p.sq_pad] = make_float2(z0, cc);
       uint32_t dso[16];
 #pragma unroll
       for (int j2 = 0; j2 < 16; ++j2) {
@@ -566,6 +644,12 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
         const float2 m = __fmul2_rn(sp, make_float2(-slope, -slope));
         const float2 v = __ffma2_rn(m, c2, dA);                                   // dA - slope s (1 - s) c
         dso[j2] = pack2<BF16>(v.x, v.y);
+      }
+      if (STORE) {
+        uint16_t* dst = p.dsstore + tile0 + (size_t)n * (128 * 128);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          *reinterpret_cast<uint4*>(dst + u * 1024) = make_uint4(dso[4 * u], dso[4 * u + 1], dso[4 * u + 2], dso[4 * u + 3]);
       }
       // dS buffer n & 1 is free once dQ(n-2) has run
       if (n > 1) ok = mbar_wait(&dq_done[n & 1], ((n - 2) >> 1) & 1, g);
@@ -1486,6 +1570,196 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
 // ---------------------------------------------------------------------------
 int make_tmap(CUtensorMap* map, const void* base, int D, int rows, int heads, int box_rows, bool bf16);
 
+// ---------------------------------------------------------------------------
+// 3c. pass B of the stored path: dK, dV as a streaming GEMM
+//
+// One CTA per 128 keys of a kv head.  For every query head of the GQA group and
+// every query tile that sees the block, TMA brings in the (query tile, key
+// block) tiles of P and dS that pass A wrote (one 32 KB bulk copy each: pass A
+// wrote them in the core-matrix order of a no-swizzle MN-major operand), with dO
+// and Q of the query tile (TMA, 128-byte swizzle), and one thread issues
+//   dV[key][d] += P^T[key][row] dO[row][d],   dK[key][d] += dS^T[key][row] Q[row][d]
+// (M = 128 keys, N = D, K = 128 rows; both operands MN-major).  No per-score maths is left: the kernel
+// streams 64 KB of P / dS per query tile from HBM, and Q / dO tiles, which every
+// key block of the head re-reads, mostly from L2.  A ring of NSLOT slots holds
+// alternately (P, dO) and (dS, Q).  TMEM: dV [0, D), dK [D, 2D) (lanes = keys).
+// ---------------------------------------------------------------------------
+template <int D>
+struct BwdKVLayout {
+  static constexpr int NSLOT = (D == 128) ? 3 : 4;
+  static constexpr int BOX = 128 * 128;        // [128 rows][64 cols] 16-bit box, 128-byte swizzle
+  static constexpr int PT = 128 * 128 * 2;     // a P or dS tile: two 64-key boxes
+  static constexpr int QT = 128 * D * 2;       // a Q or dO tile: D / 64 boxes
+  static constexpr int SLOT = PT + QT;
+  static constexpr int OFF_BAR = NSLOT * SLOT;
+  static constexpr int NBAR = 2 * NSLOT + 2;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int BYTES = OFF_MISC + 16;
+  static constexpr int ALLOC = BYTES + 1024;
+  static constexpr int THREADS = 192;          // warps 0-3 epilogue, 4 TMA, 5 MMA
+  static constexpr int WARP_TMA = 4, WARP_MMA = 5;
+  static constexpr uint32_t TM_DV = 0, TM_DK = D, TM_COLS = (2 * D <= 128) ? 128 : 256;
+  static_assert(ALLOC <= 232448, "shared memory budget");
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(BwdKVLayout<D>::THREADS, 1)
+    coalibi_bwd_kv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                          const BwdParams p) {
+  using L = BwdKVLayout<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* slot_full = bars;
+  uint64_t* slot_empty = slot_full + L::NSLOT;
+  uint64_t* acc_done = slot_empty + L::NSLOT;
+  uint64_t* mma_idle = acc_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  int hk, blk;
+  decode_block(blockIdx.x, p.B * p.Hkv, p.n_kvtiles, hk, blk);  // hk = b * Hkv + g
+  const int b = hk / p.Hkv;
+  const int gkv = hk - b * p.Hkv;
+  const int G = p.Hq / p.Hkv;
+  const int m_start = p.causal ? blk : 0;  // first query tile that sees key tile blk
+  const int nM = max(0, p.n_qtiles - m_start);
+  const int NSTEP = 2 * G * nM;            // half-steps: (P, dO) then (dS, Q) per query tile
+  CtaGuard g{abort_flag, p.status, p.timeout_ns};
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < L::NSLOT; ++i) {
+      mbar_init(&slot_full[i], 1);
+      mbar_init(&slot_empty[i], 1);
+    }
+    mbar_init(acc_done, 1);
+    mbar_init(mma_idle, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == L::WARP_MMA) {
+    tmem_alloc(tmem_slot, L::TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == L::WARP_TMA) {
+    if (lane == 0 && NSTEP > 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmDO);
+      int issued = 0;
+      for (int i = 0; i < NSTEP; ++i) {
+        const int it = i >> 1;
+        const bool second = (i & 1) != 0;  // (dS, Q) half
+        const int hh = gkv * G + it / nM;
+        const int m = m_start + it % nM;
+        const int bhq = b * p.Hq + hh;
+        const size_t tile = (size_t)bhq * p.tiles_per_head + tile_row_start(m, p.n_kvtiles, p.causal != 0) + blk;
+        const int sl = i % L::NSLOT;
+        if (!mbar_wait(&slot_empty[sl], ((i / L::NSLOT) & 1) ^ 1, g)) break;
+        mbar_arrive_expect_tx(&slot_full[sl], L::SLOT);
+        uint8_t* dst = smem + sl * L::SLOT;
+        bulk_load(dst, (second ? p.dsstore : p.pstore) + tile * (128 * 128), L::PT, &slot_full[sl]);
+        const void* tq = second ? static_cast<const void*>(&tmQ) : static_cast<const void*>(&tmDO);
+#pragma unroll
+        for (int bx = 0; bx < D / 64; ++bx) tma_load_3d(dst + L::PT + bx * L::BOX, tq, &slot_full[sl], bx * 64, m * 128, bhq);
+        ++issued;
+      }
+      // every issued copy must land before the CTA exits
+      for (int s2 = 0; s2 < L::NSLOT; ++s2) {
+        const int uses = (issued > s2) ? (issued - 1 - s2) / L::NSLOT + 1 : 0;
+        if (uses > 0) mbar_drain(&slot_full[s2], (uses - 1) & 1, g.timeout_ns);
+      }
+    }
+  } else if (warp == L::WARP_MMA) {
+    if (lane == 0 && NSTEP > 0) {
+      // M = 128 keys, N = D, K = 16 rows per MMA.  A = P^T / dS^T, MN-major without
+      // swizzle: core matrices of 8 rows x 8 keys, 128 bytes apart along the rows (K)
+      // and 128 x 16 = 2048 bytes apart along the keys (MN).  B = dO / Q, MN-major
+      // 128-byte swizzle (D / 64 boxes BOX bytes apart).
+      constexpr uint32_t idAcc = make_idesc_f16(BF16, 128, D, true, true);
+      const uint32_t base = smem_u32(smem);
+      bool ok = true;
+      for (int i = 0; i < NSTEP && ok; ++i) {
+        const int sl = i % L::NSLOT;
+        if (!(ok = mbar_wait(&slot_full[sl], (i / L::NSLOT) & 1, g))) break;
+        tc_fence_after();
+        const uint32_t a = base + sl * L::SLOT;
+        const uint32_t bq = a + L::PT;
+        const uint32_t dst = tmem + ((i & 1) ? L::TM_DK : L::TM_DV);
+        const uint32_t acc = (i >= 2) ? 1u : 0u;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          umma_ss(dst, make_sdesc_noswz(a + kk * 256, 128, 2048), make_sdesc_sw128(bq + kk * 16 * 128, L::BOX, 1024),
+                  idAcc, (acc || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&slot_empty[sl]);
+      }
+      if (ok) umma_commit(acc_done);
+      umma_commit(mma_idle);
+      mbar_drain(mma_idle, 0, g.timeout_ns);
+    }
+  } else {
+    // epilogue: thread t = key key0 + t of the block, columns = d
+    const int quarter = warp & 3;
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+    const int key = blk * 128 + (int)threadIdx.x;
+    uint8_t* dvrow = static_cast<uint8_t*>(p.dv) + ((size_t)hk * p.Skv + key) * D * 2;
+    uint8_t* dkrow = static_cast<uint8_t*>(p.dk) + ((size_t)hk * p.Skv + key) * D * 2;
+    if (NSTEP > 0) {
+      bool ok = mbar_wait(acc_done, 0, g);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        tc_fence_after();
+        const float sc = p.sm_scale;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t rv[32], rk[32];
+          tmem_ld32(lane_base + L::TM_DV + c * 32, rv);
+          tmem_ld32(lane_base + L::TM_DK + c * 32, rk);
+          tmem_ld_wait32(rv);
+          tmem_ld_fence32(rk);
+          if (key < p.Skv) {
+#pragma unroll
+            for (int v4 = 0; v4 < 4; ++v4) {
+              uint4 a, bb;
+              a.x = pack2<BF16>(__uint_as_float(rv[8 * v4 + 0]), __uint_as_float(rv[8 * v4 + 1]));
+              a.y = pack2<BF16>(__uint_as_float(rv[8 * v4 + 2]), __uint_as_float(rv[8 * v4 + 3]));
+              a.z = pack2<BF16>(__uint_as_float(rv[8 * v4 + 4]), __uint_as_float(rv[8 * v4 + 5]));
+              a.w = pack2<BF16>(__uint_as_float(rv[8 * v4 + 6]), __uint_as_float(rv[8 * v4 + 7]));
+              bb.x = pack2<BF16>(__uint_as_float(rk[8 * v4 + 0]) * sc, __uint_as_float(rk[8 * v4 + 1]) * sc);
+              bb.y = pack2<BF16>(__uint_as_float(rk[8 * v4 + 2]) * sc, __uint_as_float(rk[8 * v4 + 3]) * sc);
+              bb.z = pack2<BF16>(__uint_as_float(rk[8 * v4 + 4]) * sc, __uint_as_float(rk[8 * v4 + 5]) * sc);
+              bb.w = pack2<BF16>(__uint_as_float(rk[8 * v4 + 6]) * sc, __uint_as_float(rk[8 * v4 + 7]) * sc);
+              reinterpret_cast<uint4*>(dvrow + c * 64)[v4] = a;
+              reinterpret_cast<uint4*>(dkrow + c * 64)[v4] = bb;
+            }
+          }
+        }
+      }
+    } else if (key < p.Skv) {
+      // no query row sees these keys: their gradients are zero
+      for (int v4 = 0; v4 < D / 8; ++v4) {
+        reinterpret_cast<uint4*>(dvrow)[v4] = make_uint4(0, 0, 0, 0);
+        reinterpret_cast<uint4*>(dkrow)[v4] = make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == L::WARP_MMA) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TM_COLS);
+  }
+}
+
 template <typename K>
 inline bool bwd_set_smem_one(K kernel, int bytes) {
   return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess;
@@ -1493,10 +1767,18 @@ inline bool bwd_set_smem_one(K kernel, int bytes) {
 
 inline bool bwd_set_smem_attributes() {
   bool ok = true;
-  ok &= bwd_set_smem_one(coalibi_bwd_a_kernel<128, false>, BwdALayout<128>::ALLOC);
-  ok &= bwd_set_smem_one(coalibi_bwd_a_kernel<128, true>, BwdALayout<128>::ALLOC);
-  ok &= bwd_set_smem_one(coalibi_bwd_a_kernel<64, false>, BwdALayout<64>::ALLOC);
-  ok &= bwd_set_smem_one(coalibi_bwd_a_kernel<64, true>, BwdALayout<64>::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_a_kernel<128, false, false>, BwdALayout<128>::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_a_kernel<128, true, false>, BwdALayout<128>::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_a_kernel<64, false, false>, BwdALayout<64>::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_a_kernel<64, true, false>, BwdALayout<64>::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_a_kernel<128, false, true>, BwdALayout<128>::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_a_kernel<128, true, true>, BwdALayout<128>::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_a_kernel<64, false, true>, BwdALayout<64>::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_a_kernel<64, true, true>, BwdALayout<64>::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_kv_kernel<128, false>, BwdKVLayout<128>::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_kv_kernel<128, true>, BwdKVLayout<128>::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_kv_kernel<64, false>, BwdKVLayout<64>::ALLOC);
+  ok &= bwd_set_smem_one(coalibi_bwd_kv_kernel<64, true>, BwdKVLayout<64>::ALLOC);
   ok &= bwd_set_smem_one(coalibi_bwd_b128_kernel<false>, BwdB128Layout::ALLOC);
   ok &= bwd_set_smem_one(coalibi_bwd_b128_kernel<true>, BwdB128Layout::ALLOC);
   ok &= bwd_set_smem_one(coalibi_bwd_b_kernel<64, false>, BwdBLayout<64>::ALLOC);
@@ -1517,8 +1799,12 @@ inline int bwd_launch_t(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigne
   p.dq = a.dq;
   p.dk = a.dk;
   p.dv = a.dv;
-  p.delta = reinterpret_cast<float*>(static_cast<uint8_t*>(a.workspace) + ws.delta_off);
-  p.carry = reinterpret_cast<float2*>(static_cast<uint8_t*>(a.workspace) + ws.carry_off);
+  uint8_t* wsb = static_cast<uint8_t*>(a.workspace);
+  p.delta = reinterpret_cast<float*>(wsb + ws.delta_off);
+  p.carry = ws.stored ? nullptr : reinterpret_cast<float2*>(wsb + ws.carry_off);
+  p.pstore = ws.stored ? reinterpret_cast<uint16_t*>(wsb + ws.p_off) : nullptr;
+  p.dsstore = ws.stored ? reinterpret_cast<uint16_t*>(wsb + ws.ds_off) : nullptr;
+  p.tiles_per_head = ws.tiles_per_head;
   p.B = a.B;
   p.Hq = a.Hq;
   p.Hkv = a.Hkv;
@@ -1544,16 +1830,24 @@ inline int bwd_launch_t(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigne
   if ((rc = make_tmap(&tdo, a.dout, D, a.Sq, a.B * a.Hq, 128, BF16))) return rc;
   if ((rc = make_tmap(&tk, a.k, D, a.Skv, a.B * a.Hkv, 128, BF16))) return rc;
   if ((rc = make_tmap(&tv, a.v, D, a.Skv, a.B * a.Hkv, 128, BF16))) return rc;
-  if ((rc = make_tmap(&tkb, a.k, D, a.Skv, a.B * a.Hkv, kb_b, BF16))) return rc;
-  if ((rc = make_tmap(&tvb, a.v, D, a.Skv, a.B * a.Hkv, kb_b, BF16))) return rc;
+  if (!ws.stored) {
+    if ((rc = make_tmap(&tkb, a.k, D, a.Skv, a.B * a.Hkv, kb_b, BF16))) return rc;
+    if ((rc = make_tmap(&tvb, a.v, D, a.Skv, a.B * a.Hkv, kb_b, BF16))) return rc;
+  }
 
   const long long rows = (long long)a.B * a.Hq * p.sq_pad;
   if (phases & 1)
     coalibi_bwd_delta_kernel<D, BF16><<<(unsigned)((rows + 8 * (256 / D) - 1) / (8 * (256 / D))), 256, 0, stream>>>(p);
-  if (phases & 2)
-    coalibi_bwd_a_kernel<D, BF16><<<a.B * a.Hq * p.n_qtiles, BwdALayout<D>::THREADS, BwdALayout<D>::ALLOC,
-                                    stream>>>(tq, tdo, tk, tv, p);
-  if (phases & 4) {
+  if ((phases & 2) && ws.stored)
+    coalibi_bwd_a_kernel<D, BF16, true><<<a.B * a.Hq * p.n_qtiles, BwdALayout<D>::THREADS, BwdALayout<D>::ALLOC,
+                                          stream>>>(tq, tdo, tk, tv, p);
+  if ((phases & 2) && !ws.stored)
+    coalibi_bwd_a_kernel<D, BF16, false><<<a.B * a.Hq * p.n_qtiles, BwdALayout<D>::THREADS, BwdALayout<D>::ALLOC,
+                                           stream>>>(tq, tdo, tk, tv, p);
+  if ((phases & 4) && ws.stored) {
+    coalibi_bwd_kv_kernel<D, BF16><<<a.B * a.Hkv * p.n_kvtiles, BwdKVLayout<D>::THREADS, BwdKVLayout<D>::ALLOC,
+                                     stream>>>(tq, tdo, p);
+  } else if (phases & 4) {
     if constexpr (D == 128)
       coalibi_bwd_b128_kernel<BF16>
           <<<a.B * a.Hkv * p.n_blocks, BwdB128Layout::THREADS, BwdB128Layout::ALLOC, stream>>>(tq, tdo, tkb, tvb, p);

@@ -62,6 +62,56 @@ int make_tmap(CUtensorMap* map, const void* base, int D, int rows, int heads, in
   return COALIBI_OK;
 }
 
+// Driver entry points used to bind and restore contexts.  Binding goes through
+// the driver API so that the runtime's per-thread device selection (what
+// cudaSetDevice changes) is never touched: a thread that had no context current
+// still has none afterwards, and one that had selected device 0 still has.
+struct DrvFns {
+  PFN_cuCtxGetCurrent_v4000 ctx_get = nullptr;
+  PFN_cuCtxSetCurrent_v4000 ctx_set = nullptr;
+  PFN_cuCtxGetDevice_v2000 ctx_device = nullptr;
+  PFN_cuDeviceGet_v2000 device_get = nullptr;
+  PFN_cuDevicePrimaryCtxRetain_v7000 primary_retain = nullptr;
+  PFN_cuPointerGetAttributes_v7000 ptr_attrs = nullptr;
+  bool ok = false;
+};
+
+template <typename F>
+static void load_entry(const char* name, F& fn) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+    fn = reinterpret_cast<F>(p);
+}
+
+static const DrvFns& drv() {
+  static DrvFns f;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    load_entry("cuCtxGetCurrent", f.ctx_get);
+    load_entry("cuCtxSetCurrent", f.ctx_set);
+    load_entry("cuCtxGetDevice", f.ctx_device);
+    load_entry("cuDeviceGet", f.device_get);
+    load_entry("cuDevicePrimaryCtxRetain", f.primary_retain);
+    load_entry("cuPointerGetAttributes", f.ptr_attrs);
+    f.ok = f.ctx_get && f.ctx_set && f.ctx_device && f.device_get && f.primary_retain && f.ptr_attrs;
+  });
+  return f;
+}
+
+CtxGuard::CtxGuard() {
+  const DrvFns& f = drv();
+  if (f.ok) saved_ok_ = f.ctx_get(&saved_) == CUDA_SUCCESS;
+}
+
+CtxGuard::~CtxGuard() {
+  if (!saved_ok_) return;
+  const DrvFns& f = drv();
+  CUcontext now = nullptr;
+  if (f.ctx_get(&now) == CUDA_SUCCESS && now == saved_) return;
+  f.ctx_set(saved_);
+}
+
 namespace {
 
 constexpr int kMaxDevices = 64;
@@ -80,23 +130,53 @@ bool set_smem(K kernel, int bytes) {
   return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess;
 }
 
-// Make the device that owns `ptr` current on the calling thread and bind its
-// primary context.  Callers such as autograd's backward worker threads may
-// reach us with no context current, which the tensor-map encoder rejects.
+// Primary context of each device, retained once and kept for the life of the
+// process (as the runtime keeps it).
+struct PrimaryCtx {
+  std::once_flag once;
+  CUcontext ctx = nullptr;
+};
+PrimaryCtx g_primary[kMaxDevices];
+
+// Make a context of the device that owns `ptr` current on the calling thread: the
+// caller's own context when it is already on that device, else the device's
+// primary context (the one the runtime and PyTorch use).  Callers such as
+// autograd's backward worker threads may reach us with no context current, which
+// the tensor-map encoder rejects.  The entry point's CtxGuard undoes the switch.
 int bind_device(const void* ptr) {
-  cudaPointerAttributes attr;
-  if (cudaPointerGetAttributes(&attr, ptr) != cudaSuccess) {
-    cudaGetLastError();
-    snprintf(g_last_error, sizeof(g_last_error), "cudaPointerGetAttributes failed for %p", ptr);
+  const DrvFns& f = drv();
+  if (!f.ok) {
+    snprintf(g_last_error, sizeof(g_last_error), "CUDA driver entry points unavailable");
     return COALIBI_ERR_DEVICE;
   }
-  if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged) {
-    snprintf(g_last_error, sizeof(g_last_error), "%p is not a device pointer", ptr);
+  CUpointer_attribute names[3] = {CU_POINTER_ATTRIBUTE_MEMORY_TYPE, CU_POINTER_ATTRIBUTE_DEVICE_ORDINAL,
+                                  CU_POINTER_ATTRIBUTE_IS_MANAGED};
+  unsigned int mem_type = 0;
+  int ordinal = -1;
+  unsigned int managed = 0;
+  void* vals[3] = {&mem_type, &ordinal, &managed};
+  if (f.ptr_attrs(3, names, vals, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) {
+    snprintf(g_last_error, sizeof(g_last_error), "cuPointerGetAttributes failed for %p", ptr);
     return COALIBI_ERR_DEVICE;
   }
-  if (cudaSetDevice(attr.device) != cudaSuccess) {
-    cudaGetLastError();
-    snprintf(g_last_error, sizeof(g_last_error), "cudaSetDevice(%d) failed", attr.device);
+  if ((mem_type != CU_MEMORYTYPE_DEVICE && !managed) || ordinal < 0 || ordinal >= kMaxDevices) {
+    snprintf(g_last_error, sizeof(g_last_error), "%p is not device memory", ptr);
+    return COALIBI_ERR_DEVICE;
+  }
+  CUcontext cur = nullptr;
+  CUdevice cur_dev = -1;
+  if (f.ctx_get(&cur) == CUDA_SUCCESS && cur != nullptr && f.ctx_device(&cur_dev) == CUDA_SUCCESS) {
+    CUdevice want = -1;
+    if (f.device_get(&want, ordinal) == CUDA_SUCCESS && want == cur_dev) return COALIBI_OK;
+  }
+  PrimaryCtx& pc = g_primary[ordinal];
+  std::call_once(pc.once, [&pc, &f, ordinal] {
+    CUdevice d;
+    CUcontext c = nullptr;
+    if (f.device_get(&d, ordinal) == CUDA_SUCCESS && f.primary_retain(&c, d) == CUDA_SUCCESS) pc.ctx = c;
+  });
+  if (pc.ctx == nullptr || f.ctx_set(pc.ctx) != CUDA_SUCCESS) {
+    snprintf(g_last_error, sizeof(g_last_error), "cannot make device %d's primary context current", ordinal);
     return COALIBI_ERR_DEVICE;
   }
   return COALIBI_OK;
@@ -138,43 +218,6 @@ int device_setup(const void* ptr) {
 }
 
 }  // namespace
-
-// Driver entry points for saving / restoring the thread's current context (the
-// runtime API has no call that makes "no context" current again).
-struct CtxFns {
-  PFN_cuCtxGetCurrent_v4000 get = nullptr;
-  PFN_cuCtxSetCurrent_v4000 set = nullptr;
-};
-
-static const CtxFns& ctx_fns() {
-  static CtxFns fns;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fns.get = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
-    p = nullptr;
-    if (cudaGetDriverEntryPoint("cuCtxSetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fns.set = reinterpret_cast<PFN_cuCtxSetCurrent_v4000>(p);
-  });
-  return fns;
-}
-
-CtxGuard::CtxGuard() {
-  const CtxFns& f = ctx_fns();
-  if (f.get != nullptr && f.set != nullptr) saved_ok_ = f.get(&saved_) == CUDA_SUCCESS;
-}
-
-CtxGuard::~CtxGuard() {
-  if (!saved_ok_) return;
-  CUcontext now = nullptr;
-  const CtxFns& f = ctx_fns();
-  if (f.get(&now) == CUDA_SUCCESS && now == saved_) return;
-  f.set(saved_);
-}
 
 int enter_device(const void* ptr, void* stream) {
   if (int rc = device_setup(ptr)) return rc;
@@ -401,7 +444,22 @@ extern "C" size_t coalibi_bwd_workspace_bytes(int B, int Hq, int Hkv, int Sq, in
   (void)Hkv;
   (void)D;
   if (B <= 0 || Hq <= 0 || Sq <= 0 || Skv <= 0) return 0;
-  return bwd_workspace_layout(B, Hq, Sq, Skv).total;
+  // enough for either mask (the non-causal problem has every tile visible)
+  const size_t c = bwd_workspace_preferred(B, Hq, Sq, Skv, true);
+  const size_t n = bwd_workspace_preferred(B, Hq, Sq, Skv, false);
+  return c > n ? c : n;
+}
+
+extern "C" size_t coalibi_bwd_workspace_size(const CoalibiBwdArgs* a) {
+  if (a == nullptr || a->B <= 0 || a->Hq <= 0 || a->Sq <= 0 || a->Skv <= 0) return 0;
+  return bwd_workspace_preferred(a->B, a->Hq, a->Sq, a->Skv, a->causal != 0);
+}
+
+extern "C" size_t coalibi_bwd_workspace_min_bytes(int B, int Hq, int Hkv, int Sq, int Skv, int D) {
+  (void)Hkv;
+  (void)D;
+  if (B <= 0 || Hq <= 0 || Sq <= 0 || Skv <= 0) return 0;
+  return bwd_workspace_recompute(B, Hq, Sq, Skv).total;
 }
 
 extern "C" int coalibi_bwd_phases(const CoalibiBwdArgs* a, int phase_mask, void* stream) {
@@ -415,8 +473,8 @@ extern "C" int coalibi_bwd_phases(const CoalibiBwdArgs* a, int phase_mask, void*
   const void* ptrs[8] = {a->q, a->k, a->v, a->o, a->dout, a->dq, a->dk, a->dv};
   for (const void* ptr : ptrs)
     if (!aligned16(ptr)) return COALIBI_ERR_ALIGNMENT;
-  const BwdWorkspace ws = bwd_workspace_layout(a->B, a->Hq, a->Sq, a->Skv);
-  if (a->workspace == nullptr || a->workspace_bytes < ws.total) return COALIBI_ERR_WORKSPACE;
+  const BwdWorkspace ws = bwd_workspace_for(a->B, a->Hq, a->Sq, a->Skv, a->causal != 0, a->workspace_bytes);
+  if (a->workspace == nullptr || ws.total == 0) return COALIBI_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0) return COALIBI_ERR_ALIGNMENT;
   CtxGuard guard;
   if ((rc = enter_device(a->q, stream))) return rc;
@@ -435,16 +493,16 @@ extern "C" int coalibi_bwd_carry(const CoalibiBwdArgs* a, const float* dA_carry_
   const void* ptrs[8] = {a->q, a->k, a->v, a->o, a->dout, a->dq, a->dk, a->dv};
   for (const void* ptr : ptrs)
     if (!aligned16(ptr)) return COALIBI_ERR_ALIGNMENT;
-  const BwdWorkspace ws = bwd_workspace_layout(a->B, a->Hq, a->Sq, a->Skv);
-  if (a->workspace == nullptr || a->workspace_bytes < ws.total) return COALIBI_ERR_WORKSPACE;
+  const BwdWorkspace ws = bwd_workspace_for(a->B, a->Hq, a->Sq, a->Skv, a->causal != 0, a->workspace_bytes);
+  if (a->workspace == nullptr || ws.total == 0) return COALIBI_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0) return COALIBI_ERR_ALIGNMENT;
   CtxGuard guard;
   if ((rc = enter_device(a->q, stream))) return rc;
   return bwd_launch(*a, ws, timeout_ns(a->timeout_ms), static_cast<cudaStream_t>(stream), 7, dA_carry_in);
 }
 
-extern "C" int coalibi_describe_launch(int which, int B, int Hq, int Hkv, int Sq, int Skv, int D, int device,
-                                       char* buf, size_t buf_len) {
+extern "C" int coalibi_describe_launch(int which, int B, int Hq, int Hkv, int Sq, int Skv, int D, int causal,
+                                       int device, char* buf, size_t buf_len) {
   if (buf == nullptr || buf_len == 0) return COALIBI_ERR_NULL_POINTER;
   buf[0] = '\0';
   CtxGuard guard;
@@ -479,14 +537,29 @@ extern "C" int coalibi_describe_launch(int which, int B, int Hq, int Hkv, int Sq
     return COALIBI_OK;
   }
   if (which == 2) {
-    const int kb = D == 128 ? BwdB128Layout::KB : BwdBLayout<64>::KB;
-    const long long nb = (Skv + kb - 1) / kb;
-    snprintf(buf, buf_len,
-             "backward: coalibi_bwd_delta_kernel<D=%d>; coalibi_bwd_a_kernel<D=%d> (query-major) grid %lld x %d "
-             "threads; %s (key-major, %d keys per CTA, GQA group of %d heads summed in TMEM) grid %lld x %d threads",
-             D, D, (long long)B * Hq * nq, D == 128 ? BwdALayout<128>::THREADS : BwdALayout<64>::THREADS,
-             D == 128 ? "coalibi_bwd_b128_kernel" : "coalibi_bwd_b_kernel<D=64>", kb, Hq / Hkv,
-             (long long)B * Hkv * nb, D == 128 ? BwdB128Layout::THREADS : BwdBLayout<64>::THREADS);
+    const BwdWorkspace st = bwd_workspace_stored(B, Hq, Sq, Skv, causal != 0);
+    const bool stored = bwd_workspace_preferred(B, Hq, Sq, Skv, causal != 0) == st.total;
+    const int athreads = D == 128 ? BwdALayout<128>::THREADS : BwdALayout<64>::THREADS;
+    if (stored) {
+      snprintf(buf, buf_len,
+               "backward, stored path (P / dS scratch %.1f MB): coalibi_bwd_delta_kernel<D=%d>; "
+               "coalibi_bwd_a_kernel<D=%d, stores P and dS> (query-major) grid %lld x %d threads; "
+               "coalibi_bwd_kv_kernel<D=%d> (streaming dV = P^T dO, dK = dS^T Q, GQA group of %d heads summed in "
+               "TMEM) grid %lld x %d threads",
+               (double)(st.total - st.p_off) / 1e6, D, D, (long long)B * Hq * nq, athreads, D, Hq / Hkv,
+               (long long)B * Hkv * ((Skv + 127) / 128), D == 128 ? BwdKVLayout<128>::THREADS : BwdKVLayout<64>::THREADS);
+    } else {
+      const int kb = D == 128 ? BwdB128Layout::KB : BwdBLayout<64>::KB;
+      const long long nb = (Skv + kb - 1) / kb;
+      snprintf(buf, buf_len,
+               "backward, recompute path (P / dS scratch would exceed the cap): coalibi_bwd_delta_kernel<D=%d>; "
+               "coalibi_bwd_a_kernel<D=%d> (query-major, carries every 32 keys) grid %lld x %d threads; %s "
+               "(key-major, recomputes S, dP, P, dS; %d keys per CTA, GQA group of %d heads summed in TMEM) grid "
+               "%lld x %d threads",
+               D, D, (long long)B * Hq * nq, athreads,
+               D == 128 ? "coalibi_bwd_b128_kernel" : "coalibi_bwd_b_kernel<D=64>", kb, Hq / Hkv,
+               (long long)B * Hkv * nb, D == 128 ? BwdB128Layout::THREADS : BwdBLayout<64>::THREADS);
+    }
     return COALIBI_OK;
   }
   return COALIBI_ERR_SHAPE;

@@ -66,7 +66,9 @@ extern "C" int coalibi_bwd_noalloc(const CoalibiBwdArgs* args, void* stream) {
   if (int rc = coalibi::check_common(args->B, args->Hq, args->Hkv, args->Sq, args->Skv, args->D, args->dtype,
                                      args->slopes_dtype))
     return rc;
-  const size_t need = coalibi_bwd_workspace_bytes(args->B, args->Hq, args->Hkv, args->Sq, args->Skv, args->D);
+  // the smallest scratch any path of the backward can run in (the path that fits
+  // the array is chosen inside coalibi_bwd)
+  const size_t need = coalibi_bwd_workspace_min_bytes(args->B, args->Hq, args->Hkv, args->Sq, args->Skv, args->D);
   if (need == 0) return COALIBI_ERR_SHAPE;
   if (need > kNoallocScratchBytes) {
     char msg[200];

@@ -95,8 +95,15 @@ int coalibi_fwd_decode(const CoalibiFwdArgs* args, void* workspace, size_t works
  * including the dk/dv partial-buffer reduction at :132-133 and, for GQA, the group
  * sum autograd performs through repeat_interleave at :145-146) and the kernel
  * co_alibi_attn/co_alibi_bwd_kernel.py:19-146.  dk and dv have Hkv heads.
- * workspace: device scratch of at least coalibi_bwd_workspace_bytes() bytes,
- * 256-byte aligned; its contents on entry do not matter. */
+ * workspace: device scratch, 256-byte aligned, its contents on entry irrelevant.
+ * The size picks the algorithm: with at least the "stored" size (what
+ * coalibi_bwd_workspace_size() returns while that stays below 24 GiB) the first
+ * kernel also writes P and dS as 16-bit 128 x 128 tiles -- 4 bytes per visible
+ * score, 4.3 GB at B8 H16 S4096 causal, half the reference's dk/dv partial
+ * buffers -- and dK, dV come from a streaming GEMM over them; with less, down to
+ * coalibi_bwd_workspace_min_bytes() (8 bytes per row per 32 keys), the second
+ * kernel recomputes P and dS instead.  Both agree with the reference within the
+ * same tolerances; less than the minimum returns COALIBI_ERR_WORKSPACE. */
 typedef struct CoalibiBwdArgs {
   const void* q;
   const void* k;
@@ -120,7 +127,17 @@ typedef struct CoalibiBwdArgs {
   unsigned int timeout_ms;
 } CoalibiBwdArgs;
 
+/* Workspace size to allocate for this call's problem and mask (args->B, Hq, Hkv,
+ * Sq, Skv, D, causal; the pointers are not read): the stored layout while its
+ * P / dS scratch stays below 24 GiB, else the recompute layout. */
+size_t coalibi_bwd_workspace_size(const CoalibiBwdArgs* args);
+
+/* A size that serves either mask of the problem (the larger of the two
+ * coalibi_bwd_workspace_size values). */
 size_t coalibi_bwd_workspace_bytes(int B, int Hq, int Hkv, int Sq, int Skv, int D);
+
+/* The smallest workspace coalibi_bwd accepts for the problem (the recompute layout). */
+size_t coalibi_bwd_workspace_min_bytes(int B, int Hq, int Hkv, int Sq, int Skv, int D);
 
 int coalibi_bwd(const CoalibiBwdArgs* args, void* stream);
 
@@ -135,7 +152,8 @@ int coalibi_bwd_carry(const CoalibiBwdArgs* args, const float* dA_carry_in, void
 
 /* Profiling aid with no counterpart in the reference: launch only the backward
  * kernels selected by phase_mask (bit 0: delta = rowsum(dO * O) pre-pass, bit 1:
- * pass A -> dq and the per-32-key carries in the workspace, bit 2: pass B -> dk, dv).
+ * pass A -> dq and, in the workspace, P / dS tiles or the per-32-key carries,
+ * bit 2: pass B -> dk, dv).
  * Phases read what earlier phases wrote into the workspace, so they must run in
  * order on one stream; coalibi_bwd(args, s) == coalibi_bwd_phases(args, 7, s). */
 int coalibi_bwd_phases(const CoalibiBwdArgs* args, int phase_mask, void* stream);
@@ -149,9 +167,10 @@ int coalibi_bwd_phases(const CoalibiBwdArgs* args, int phase_mask, void* stream)
  * memory at the call -- a plugin host or FFI caller that owns only the tensors
  * it passes, or code that must avoid cudaMalloc there because it can synchronise
  * the device.  Its scratch is one file-scope device array of
- * COALIBI_NOALLOC_SCRATCH_BYTES per GPU, held until the process exits; problems
- * needing more (coalibi_bwd_workspace_bytes() > that) return COALIBI_ERR_WORKSPACE
- * without launching.  The first call on each device looks up the array's device
+ * COALIBI_NOALLOC_SCRATCH_BYTES per GPU, held until the process exits; the
+ * backward runs the stored path when its scratch fits there, else the recompute
+ * path; problems needing more (coalibi_bwd_workspace_min_bytes() > that) return
+ * COALIBI_ERR_WORKSPACE without launching.  The first call on each device looks up the array's device
  * address (cudaGetSymbolAddress); make it before any stream capture.  The address
  * is not looked up again, so it is stale after cudaDeviceReset on that device.
  * All calls on a device share the array, so calls that overlap on the GPU race:
@@ -171,10 +190,11 @@ int coalibi_selftest_wait_timeout(unsigned int timeout_ms, int* status, void* st
  * text: the counterpart of the reference's COALIBI_VERBOSE=1 print of the
  * configuration its autotuner chose (co_alibi_attn/co_alibi_attn.py:58-63 for the
  * forward, :125-130 for the backward).  which: 0 forward (coalibi_fwd), 1 decode
- * forward (coalibi_fwd_decode), 2 backward (coalibi_bwd); device: the CUDA device
- * index (for its SM count).  Writes a NUL-terminated description into buf,
- * truncated to buf_len bytes.  Launches nothing and changes no CUDA state. */
-int coalibi_describe_launch(int which, int B, int Hq, int Hkv, int Sq, int Skv, int D, int device,
+ * forward (coalibi_fwd_decode), 2 backward (coalibi_bwd, with the workspace of
+ * coalibi_bwd_workspace_size); causal: the mask; device: the CUDA device index (for
+ * its SM count).  Writes a NUL-terminated description into buf, truncated to
+ * buf_len bytes.  Launches nothing and changes no CUDA state. */
+int coalibi_describe_launch(int which, int B, int Hq, int Hkv, int Sq, int Skv, int D, int causal, int device,
                             char* buf, size_t buf_len);
 
 /* Static name of an error code. */

@@ -33,12 +33,29 @@ def test_strerror_and_workspace_size():
     for code in range(0, 11):
         assert _lib.strerror(code)
     assert "head dim" in _lib.strerror(2)
-    # delta: float per (b, h, padded row); carries: float2 per (b, h, 32-key block, padded row)
+    # recompute layout: delta float per (b, h, padded row), carries float2 per (b, h, 32-key block, padded row)
     sq_pad, nkb = 4096, 4096 // 32
-    want = 8 * 16 * sq_pad * 4 + 8 * 16 * nkb * sq_pad * 8
-    assert lib.coalibi_bwd_workspace_bytes(8, 16, 16, 4096, 4096, 128) == want
-    assert lib.coalibi_bwd_workspace_bytes(1, 4, 4, 37, 37, 64) == 256 * ((4 * 128 * 4 + 255) // 256) + \
+    want_min = 8 * 16 * sq_pad * 4 + 8 * 16 * nkb * sq_pad * 8
+    assert lib.coalibi_bwd_workspace_min_bytes(8, 16, 16, 4096, 4096, 128) == want_min
+    assert lib.coalibi_bwd_workspace_min_bytes(1, 4, 4, 37, 37, 64) == 256 * ((4 * 128 * 4 + 255) // 256) + \
         256 * ((4 * 2 * 128 * 8 + 255) // 256)
+    # stored layout: delta, then P and dS as 32 KB tiles, one per visible (query tile, key tile) pair
+    a = _lib.CoalibiBwdArgs(B=8, Hq=16, Hkv=16, Sq=4096, Skv=4096, D=128, causal=1)
+    tiles = 32 * 33 // 2
+    want_stored = 8 * 16 * sq_pad * 4 + 2 * 8 * 16 * tiles * 32768
+    assert lib.coalibi_bwd_workspace_size(ctypes.byref(a)) == want_stored
+    a.causal = 0
+    assert lib.coalibi_bwd_workspace_size(ctypes.byref(a)) == 8 * 16 * sq_pad * 4 + 2 * 8 * 16 * 32 * 32 * 32768
+    assert lib.coalibi_bwd_workspace_bytes(8, 16, 16, 4096, 4096, 128) == lib.coalibi_bwd_workspace_size(
+        ctypes.byref(a))
+    # rectangular causal (top-left): query tile q sees key tiles 0..min(q, n_kv - 1)
+    a = _lib.CoalibiBwdArgs(B=1, Hq=2, Hkv=1, Sq=40 * 128, Skv=10 * 128, D=64, causal=1)
+    tiles = 10 * 11 // 2 + 30 * 10
+    assert lib.coalibi_bwd_workspace_size(ctypes.byref(a)) == 2 * 40 * 128 * 4 + 2 * 2 * tiles * 32768
+    # past the 24 GiB cap of the stored P / dS scratch: the recompute layout
+    a = _lib.CoalibiBwdArgs(B=1, Hq=32, Hkv=8, Sq=32768, Skv=32768, D=128, causal=1)
+    assert lib.coalibi_bwd_workspace_size(ctypes.byref(a)) == lib.coalibi_bwd_workspace_min_bytes(
+        1, 32, 8, 32768, 32768, 128)
     assert lib.coalibi_bwd_workspace_bytes(0, 4, 4, 37, 37, 64) == 0
 
 
@@ -75,6 +92,8 @@ def test_bwd_validation_and_phase_mask():
     big = _lib.CoalibiBwdArgs(**{f: getattr(a, f) for f, _ in _lib.CoalibiBwdArgs._fields_})
     big.B, big.Hq, big.Hkv, big.Sq, big.Skv, big.D = 8, 16, 16, 4096, 4096, 128
     assert lib.coalibi_bwd_noalloc(ctypes.byref(big), None) == 8  # exceeds the static scratch
+    big.workspace, big.workspace_bytes = 256, lib.coalibi_bwd_workspace_min_bytes(8, 16, 16, 4096, 4096, 128) - 1
+    assert lib.coalibi_bwd(ctypes.byref(big), None) == 8          # below the smallest (recompute) layout
     assert "static scratch" in lib.coalibi_last_error().decode()
     # invalid shapes get the same status as from coalibi_bwd, before the size check
     bad = _lib.CoalibiBwdArgs(**{f: getattr(big, f) for f, _ in _lib.CoalibiBwdArgs._fields_})
@@ -90,9 +109,9 @@ def test_describe_launch_validates_before_device_use():
     from co_alibi_attn import _lib
     lib = _lib.load()
     buf = ctypes.create_string_buffer(256)
-    assert lib.coalibi_describe_launch(0, 1, 2, 2, 128, 128, 96, 0, buf, len(buf)) == 2
-    assert lib.coalibi_describe_launch(0, 1, 6, 4, 128, 128, 128, 0, buf, len(buf)) == 4
-    assert lib.coalibi_describe_launch(0, 1, 2, 2, 128, 128, 128, 0, None, 0) == 1
+    assert lib.coalibi_describe_launch(0, 1, 2, 2, 128, 128, 96, 1, 0, buf, len(buf)) == 2
+    assert lib.coalibi_describe_launch(0, 1, 6, 4, 128, 128, 128, 1, 0, buf, len(buf)) == 4
+    assert lib.coalibi_describe_launch(0, 1, 2, 2, 128, 128, 128, 1, 0, None, 0) == 1
 
 
 def test_slope_table_matches_reference_fixture():

@@ -44,7 +44,7 @@ def _problem(dev, B=1, Hq=4, Hkv=2, S=300, D=128):
                              sm_scale=1.0 / math.sqrt(D), status=None, timeout_ms=0)
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     lib = _lib.load()
-    nbytes = lib.coalibi_bwd_workspace_bytes(B, Hq, Hkv, S, S, D)
+    nbytes = lib.coalibi_bwd_workspace_bytes(B, Hq, Hkv, S, S, D)  # enough for either mask
     ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
     ba = _lib.CoalibiBwdArgs(q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), o=o.data_ptr(), dout=do.data_ptr(),
                              lse=lse.data_ptr(), rowsig=rs.data_ptr(), slopes=slopes.data_ptr(),
@@ -89,7 +89,7 @@ def test_fresh_thread_keeps_no_context():
             seen[name] = call()
             seen[name + ":ctx"] = _current_ctx(drv)
         buf = ctypes.create_string_buffer(256)
-        seen["describe"] = lib.coalibi_describe_launch(0, 1, 4, 2, 300, 300, 128, 0, buf, len(buf))
+        seen["describe"] = lib.coalibi_describe_launch(0, 1, 4, 2, 300, 300, 128, 1, 0, buf, len(buf))
         seen["describe:ctx"] = _current_ctx(drv)
 
     t = threading.Thread(target=worker)
@@ -133,6 +133,20 @@ def test_other_device_tensors_leave_current_device():
     for name, call in _calls(lib, fa, ba, s1):
         assert call() == 0, f"{name}: {lib.coalibi_last_error().decode()}"
         assert torch.cuda.current_device() == 0 and _current_ctx(drv) == ctx0, name
+    torch.cuda.synchronize(1)
+    # a thread with no context current: afterwards still none, and the runtime's
+    # device selection of that thread is still its default (device 0)
+    seen = {}
+
+    def worker():
+        seen["rc"] = lib.coalibi_fwd(ctypes.byref(fa), s1)
+        seen["ctx"] = _current_ctx(drv)
+        seen["dev"] = torch.cuda.current_device()
+
+    t = threading.Thread(target=worker)
+    t.start()
+    t.join()
+    assert seen == {"rc": 0, "ctx": None, "dev": 0}, seen
     torch.cuda.synchronize(1)
     s0 = torch.cuda.current_stream(0).cuda_stream
     assert lib.coalibi_fwd(ctypes.byref(fa), s0) == 9  # COALIBI_ERR_DEVICE

@@ -127,6 +127,29 @@ def test_backward_gqa_ragged_long_sampled(api):
         assert e <= GRAD_REL, f"(b={b}, g={g}) {name} relative error {e:.3e}"
 
 
+RECOMPUTE_CASES = [c for i, c in enumerate(CASES) if i in (1, 3, 4, 5, 7, 8, 12)]
+
+
+@pytest.mark.parametrize("case", RECOMPUTE_CASES, ids=[_ids(c) for c in RECOMPUTE_CASES])
+def test_backward_recompute_path_matches_oracle(api, case):
+    """The backward given only its smallest workspace (coalibi_bwd_workspace_min_bytes),
+    where pass B recomputes P and dS from pass A's running sums instead of reading
+    them: the path problems whose P / dS scratch would pass the cap take."""
+    from co_alibi_attn.co_alibi_attn import _fwd, _bwd, _api_slopes
+    B, Hq, Hkv, Sq, Skv, D, causal, dtype = case
+    q, k, v, do = make_inputs(B, Hq, Hkv, Sq, Skv, D, dtype, seed=Sq * 13 + D)
+    scale = 1.0 / math.sqrt(D)
+    qc, kc, vc, doc = (t.cuda() for t in (q, k, v, do))
+    sl = _api_slopes(Hq, 8.0, dtype, qc.device)
+    o, lse, rs = _fwd(qc, kc, vc, sl, causal, scale)
+    dq, dk, dv = _bwd(qc, kc, vc, o, doc, lse, rs, sl, causal, scale, min_workspace=True)
+    torch.cuda.synchronize()
+    assert api.device_status(reset=True) == 0
+    for name, x, r in zip(("dq", "dk", "dv"), (dq, dk, dv), oracle_bwd(q, k, v, do, causal, scale)):
+        e = rel_err(x.cpu(), r)
+        assert e <= GRAD_REL, f"{name} relative error {e:.3e}"
+
+
 def test_backward_deterministic(api):
     q, k, v, do = make_inputs(1, 4, 2, 700, 700, 128, torch.float16, seed=9)
     r1 = _run(api, q, k, v, do, True, 1 / math.sqrt(128))

@@ -48,7 +48,10 @@ def test_noalloc_matches_workspace_backward(shape):
     stream = torch.cuda.current_stream().cuda_stream
 
     ref = [torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)]
-    nbytes = lib.coalibi_bwd_workspace_bytes(B, Hq, Hkv, S, S, D)
+    a = _args(_lib, q, k, v, o, do, lse, rowsig, slopes, *ref, causal)
+    nbytes = lib.coalibi_bwd_workspace_size(ctypes.byref(a))
+    # the static array holds this problem's preferred (stored P / dS) layout, so both
+    # calls run the same kernels
     assert nbytes <= _lib.NOALLOC_SCRATCH_BYTES
     ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
     a = _args(_lib, q, k, v, o, do, lse, rowsig, slopes, *ref, causal, ws)
@@ -75,7 +78,7 @@ def test_noalloc_rejects_oversized_problem():
     lib = _lib.load()
     t = torch.zeros(16, device="cuda", dtype=torch.float16)
     B, H, S, D = 8, 16, 4096, 128
-    assert lib.coalibi_bwd_workspace_bytes(B, H, H, S, S, D) > _lib.NOALLOC_SCRATCH_BYTES
+    assert lib.coalibi_bwd_workspace_min_bytes(B, H, H, S, S, D) > _lib.NOALLOC_SCRATCH_BYTES
     a = _lib.CoalibiBwdArgs(q=t.data_ptr(), k=t.data_ptr(), v=t.data_ptr(), o=t.data_ptr(),
                             dout=t.data_ptr(), lse=t.data_ptr(), rowsig=t.data_ptr(), slopes=t.data_ptr(),
                             dq=t.data_ptr(), dk=t.data_ptr(), dv=t.data_ptr(), workspace=None,
