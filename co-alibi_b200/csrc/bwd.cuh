@@ -79,19 +79,19 @@ inline BwdWorkspace bwd_workspace_recompute(int B, int Hq, int Sq, int Skv) {
   return w;
 }
 
-// stored: delta float [B*Hq][sq_pad]; P, dS 16-bit [B*Hq][tiles_per_head][16][128][8]: each tile
-// in 8-key segments of all 128 rows (the no-swizzle core-matrix order the MMA reads)
+// stored: delta float [B*Hq][sq_pad]; then per visible tile a P tile and its dS tile, 16-bit
+// [B*Hq][tiles_per_head][P, dS][16][128][8]: each tile in 8-key segments of all 128 rows
+// (the no-swizzle core-matrix order the MMA reads)
 inline BwdWorkspace bwd_workspace_stored(int B, int Hq, int Sq, int Skv, bool causal) {
   const int n_q = (Sq + 127) / 128, n_kv = (Skv + 127) / 128;
   const size_t sq_pad = (size_t)n_q * 128;
   BwdWorkspace w{};
   w.stored = true;
   w.tiles_per_head = tile_row_start(n_q, n_kv, causal);
-  const size_t pbytes = (size_t)B * Hq * (size_t)w.tiles_per_head * kTileBytes;
   w.delta_off = 0;
   w.p_off = align256((size_t)B * Hq * sq_pad * 4);
-  w.ds_off = w.p_off + pbytes;
-  w.total = w.ds_off + pbytes;
+  w.ds_off = w.p_off + kTileBytes;  // dS tile right after its P tile
+  w.total = w.p_off + 2 * (size_t)B * Hq * (size_t)w.tiles_per_head * kTileBytes;
   return w;
 }
 
@@ -124,8 +124,7 @@ struct BwdParams {
   void* dv;
   float* delta;
   float2* carry;     // recompute path: pass A -> pass B running sums (null on the stored path)
-  uint16_t* pstore;  // stored path: P tiles [B*Hq][tiles_per_head][16][128][8] (null on the recompute path)
-  uint16_t* dsstore; // stored path: dS tiles, same layout
+  uint16_t* pstore;  // stored path: [B*Hq][tiles_per_head][P, dS][16][128][8] (null on the recompute path)
   long long tiles_per_head;
   int B, Hq, Hkv, Sq, Skv;
   int slopes_dtype;
@@ -264,6 +263,9 @@ struct BwdALayout {
   static constexpr int WARP_TMA = 4 * NWG, WARP_MMA = 4 * NWG + 1;
   static constexpr int REGS_SOFTMAX = 104, REGS_PRODUCER = 64;
   static_assert(4 * REGS_SOFTMAX + REGS_PRODUCER <= 5 * 96, "register split exceeds the launch allocation");
+  // the variant that also stores P and dS holds more per thread: 112 / 32
+  static constexpr int REGS_SOFTMAX_ST = 112, REGS_PRODUCER_ST = 32;
+  static_assert(4 * REGS_SOFTMAX_ST + REGS_PRODUCER_ST <= 5 * 96, "register split exceeds the launch allocation");
   static constexpr uint32_t TM_S = 0, TM_DP = 128, TM_DS = 256, TM_DQ = 384, TM_COLS = 512;
   static_assert(ALLOC <= 232448, "shared memory budget");
   static_assert(TM_DQ + D <= TM_COLS, "TMEM budget");
@@ -407,7 +409,7 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp >= L::WARP_TMA) {
-    regs_decrease<L::REGS_PRODUCER>();
+    regs_decrease<STORE ? L::REGS_PRODUCER_ST : L::REGS_PRODUCER>();
   if (warp == L::WARP_TMA) {
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
@@ -529,7 +531,7 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
     }
   }
   } else {
-    regs_increase<L::REGS_SOFTMAX>();
+    regs_increase<STORE ? L::REGS_SOFTMAX_ST : L::REGS_SOFTMAX>();
     // ------------------------------------------------------------ softmax: 4 x 32 keys per row
     const int wg = warp >> 2;
     const int quarter = warp & 3;
@@ -552,9 +554,10 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
     // stored path: row t_row of the (qt, n) P / dS tiles; a tile holds 16 segments of
     // 8 keys x 128 rows, so this thread's 32 keys are segments 4 wg .. 4 wg + 3 and a
     // warp (32 consecutive rows) writes 512 contiguous bytes per segment
-    const size_t tile0 = STORE ? ((size_t)bh * p.tiles_per_head + tile_row_start(qt, p.n_kvtiles, p.causal != 0)) *
-                                     (size_t)(128 * 128) + (size_t)(4 * wg * 128 + t_row) * 8
-                               : 0;
+    uint16_t* const pd_row =
+        STORE ? p.pstore + ((size_t)bh * p.tiles_per_head + tile_row_start(qt, p.n_kvtiles, p.causal != 0)) *
+                               (size_t)(2 * 128 * 128) + (4 * wg * 128 + t_row) * 8
+              : nullptr;
     bool ok = true;
     for (int n = 0; n < N; ++n) {
       const int key0 = n * BN + 32 * wg;  // first key of this thread's chunk
@@ -609,9 +612,9 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
                          : bwd_a_da<false, BF16, STORE>(xa + 16 * hh, sg + 16 * hh, dpr, key0 + 16 * hh, lim, slope2,
                                                         delta, zz, pk);
           if (STORE) {
-            uint16_t* dst = p.pstore + tile0 + (size_t)n * (128 * 128) + (2 * hh) * 1024;
-            *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            *reinterpret_cast<uint4*>(dst + 1024) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+            uint16_t* dst = pd_row + n * (2 * 128 * 128) + (2 * hh) * 1024;
+            st_global_na(dst, make_uint4(pk[0], pk[1], pk[2], pk[3]));
+            st_global_na(dst + 1024, make_uint4(pk[4], pk[5], pk[6], pk[7]));
           }
         }
       }
@@ -646,10 +649,10 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
         dso[j2] = pack2<BF16>(v.x, v.y);
       }
       if (STORE) {
-        uint16_t* dst = p.dsstore + tile0 + (size_t)n * (128 * 128);
+        uint16_t* dst = pd_row + n * (2 * 128 * 128) + 128 * 128;
 #pragma unroll
         for (int u = 0; u < 4; ++u)
-          *reinterpret_cast<uint4*>(dst + u * 1024) = make_uint4(dso[4 * u], dso[4 * u + 1], dso[4 * u + 2], dso[4 * u + 3]);
+          st_global_na(dst + u * 1024, make_uint4(dso[4 * u], dso[4 * u + 1], dso[4 * u + 2], dso[4 * u + 3]));
       }
       // dS buffer n & 1 is free once dQ(n-2) has run
       if (n > 1) ok = mbar_wait(&dq_done[n & 1], ((n - 2) >> 1) & 1, g);
@@ -1664,7 +1667,7 @@ __global__ void __launch_bounds__(BwdKVLayout<D>::THREADS, 1)
         if (!mbar_wait(&slot_empty[sl], ((i / L::NSLOT) & 1) ^ 1, g)) break;
         mbar_arrive_expect_tx(&slot_full[sl], L::SLOT);
         uint8_t* dst = smem + sl * L::SLOT;
-        bulk_load(dst, (second ? p.dsstore : p.pstore) + tile * (128 * 128), L::PT, &slot_full[sl]);
+        bulk_load(dst, p.pstore + (2 * tile + (second ? 1 : 0)) * (128 * 128), L::PT, &slot_full[sl]);
         const void* tq = second ? static_cast<const void*>(&tmQ) : static_cast<const void*>(&tmDO);
 #pragma unroll
         for (int bx = 0; bx < D / 64; ++bx) tma_load_3d(dst + L::PT + bx * L::BOX, tq, &slot_full[sl], bx * 64, m * 128, bhq);
@@ -1803,7 +1806,6 @@ inline int bwd_launch_t(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigne
   p.delta = reinterpret_cast<float*>(wsb + ws.delta_off);
   p.carry = ws.stored ? nullptr : reinterpret_cast<float2*>(wsb + ws.carry_off);
   p.pstore = ws.stored ? reinterpret_cast<uint16_t*>(wsb + ws.p_off) : nullptr;
-  p.dsstore = ws.stored ? reinterpret_cast<uint16_t*>(wsb + ws.ds_off) : nullptr;
   p.tiles_per_head = ws.tiles_per_head;
   p.B = a.B;
   p.Hq = a.Hq;

@@ -374,6 +374,14 @@ __device__ __forceinline__ float2 ldg_pinned(const float2* p) {
   return v;
 }
 
+// 16-byte global store that does not allocate in L1 (streamed output: keeps the
+// small L1 that a large shared-memory carve-out leaves for the data that reuses it).
+__device__ __forceinline__ void st_global_na(void* p, uint4 v) {
+  asm volatile("st.global.L1::no_allocate.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
 // ----------------------------------------------------------------------------
 // Scalar helpers
 // ----------------------------------------------------------------------------
