@@ -237,6 +237,11 @@ __device__ __forceinline__ void bwd_chunk(const uint32_t* sreg, const uint32_t* 
 // dS (packed 16-bit, two buffers so the softmax never waits for the previous
 // sub-tile's dQ) [256,384), dQ [384,384+D).
 // ---------------------------------------------------------------------------
+#ifndef COALIBI_PASS_A_IDLE_NS
+#define COALIBI_PASS_A_IDLE_NS 60
+#endif
+constexpr unsigned kPassAIdleNs = COALIBI_PASS_A_IDLE_NS;  // pass A MMA issuer: sleep when nothing is ready
+
 template <int D>
 struct BwdALayout {
   static constexpr int BM = 128, BN = 128;
@@ -514,6 +519,9 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
           idle = 0;
           t_idle = 0;
         } else {
+          // suspend briefly: a spinning issuer takes issue slots from the four softmax
+          // warps that share its sub-partition
+          if (kPassAIdleNs > 0) __nanosleep(kPassAIdleNs);
           if (++idle == 64) {
             idle = 0;
             const uint64_t now = global_timer_ns();

@@ -100,16 +100,21 @@ struct FwdLayout {
   static_assert(ALLOC <= 232448, "shared memory budget");
 };
 
-// Sigmoids, local suffix sums and penalised log2-domain logits of one 32-key
-// chunk (raw q.k dot products in sreg[0..31], keys key0..key0+31), right to
-// left, starting the suffix sum at 0.  Writes a' = c_a x - slope2 * local_suffix
-// back into sreg[]; returns the chunk's sigmoid total and the max of a'.
+// Sigmoids, suffix sums and penalised log2-domain logits of one 32-key chunk (raw
+// q.k dot products in sreg[0..31], keys key0..key0+31), right to left, as four
+// 8-key sub-chunks whose suffix sums each start at 0: four short dependent add
+// chains, two in flight at a time, instead of one of 32.  Writes
+// a'_j = c_a x_j - slope2 * (sigmoid suffix of key j within its sub-chunk) back into
+// sreg[].  The sub-chunks right of sub-chunk k add their sigmoid totals to every
+// suffix in it; the caller folds that into the sub-chunk's exponent shift,
+// soff[k] = slope2 * (sigmoid total of sub-chunks k+1..3), so no per-key work is
+// added.  Returns (chunk sigmoid total, max over the chunk of a' - soff).
 template <bool MASK>
 __device__ __forceinline__ float2 fwd_scan_chunk(uint32_t* sreg, int key0, int lim, float c_t, float c_a,
-                                                 float slope2) {
-  float run = 0.f, mx = -INFINITY;
+                                                 float slope2, float* soff) {
+  float tot[4], mxk[4];
 #pragma unroll
-  for (int c = 1; c >= 0; --c) {  // 16-key groups, right to left
+  for (int c = 1; c >= 0; --c) {  // 16-key groups (sub-chunks 2c+1 and 2c), right to left
     float sg[16];
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
@@ -121,24 +126,39 @@ __device__ __forceinline__ float2 fwd_scan_chunk(uint32_t* sreg, int key0, int l
       sg[2 * q] = (MASK && key0 + j >= lim) ? 0.f : s.x;
       sg[2 * q + 1] = (MASK && key0 + j + 1 >= lim) ? 0.f : s.y;
     }
+    float run[2] = {0.f, 0.f}, m[2] = {-INFINITY, -INFINITY};  // [0]: sub-chunk 2c, [1]: 2c + 1
 #pragma unroll
-    for (int q = 7; q >= 0; --q) {
-      const int j = 16 * c + 2 * q;
-      run += sg[2 * q + 1];
-      const float r1 = run;
-      run += sg[2 * q];
-      const float r0 = run;
-      const float2 xa = __fmul2_rn(make_float2(__uint_as_float(sreg[j]), __uint_as_float(sreg[j + 1])),
-                                   make_float2(c_a, c_a));
-      float2 a = __ffma2_rn(make_float2(-slope2, -slope2), make_float2(r0, r1), xa);
-      if (MASK && key0 + j >= lim) a.x = -INFINITY;
-      if (MASK && key0 + j + 1 >= lim) a.y = -INFINITY;
-      mx = max3(mx, a.x, a.y);
-      sreg[j] = __float_as_uint(a.x);
-      sreg[j + 1] = __float_as_uint(a.y);
+    for (int q = 3; q >= 0; --q) {
+#pragma unroll
+      for (int h = 1; h >= 0; --h) {
+        const int qq = q + 4 * h;  // pair within the 16-key group
+        const int j = 16 * c + 2 * qq;
+        run[h] += sg[2 * qq + 1];
+        const float r1 = run[h];
+        run[h] += sg[2 * qq];
+        const float r0 = run[h];
+        const float2 xa = __fmul2_rn(make_float2(__uint_as_float(sreg[j]), __uint_as_float(sreg[j + 1])),
+                                     make_float2(c_a, c_a));
+        float2 a = __ffma2_rn(make_float2(-slope2, -slope2), make_float2(r0, r1), xa);
+        if (MASK && key0 + j >= lim) a.x = -INFINITY;
+        if (MASK && key0 + j + 1 >= lim) a.y = -INFINITY;
+        m[h] = max3(m[h], a.x, a.y);
+        sreg[j] = __float_as_uint(a.x);
+        sreg[j + 1] = __float_as_uint(a.y);
+      }
     }
+    tot[2 * c] = run[0];
+    tot[2 * c + 1] = run[1];
+    mxk[2 * c] = m[0];
+    mxk[2 * c + 1] = m[1];
   }
-  return make_float2(run, mx);
+  const float o2 = tot[3], o1 = o2 + tot[2], o0 = o1 + tot[1];
+  soff[3] = 0.f;
+  soff[2] = slope2 * o2;
+  soff[1] = slope2 * o1;
+  soff[0] = slope2 * o0;
+  const float mx = fmaxf(fmaxf(mxk[3], mxk[2] - soff[2]), fmaxf(mxk[1] - soff[1], mxk[0] - soff[0]));
+  return make_float2(o0 + tot[0], mx);
 }
 
 // A CTA's work list: in round r it takes item r * G + c (c = blockIdx.x, G =
@@ -405,14 +425,15 @@ __global__ void __launch_bounds__(640, 1)
         if (ok) ok = mbar_wait(&s_full[tg & 1], (tg >> 1) & 1, g);
         ok = __all_sync(0xffffffffu, ok);
         uint32_t sreg[32];
+        float soff[4];  // per-sub-chunk exponent shifts from fwd_scan_chunk
         float2 loc = make_float2(0.f, -INFINITY);
         if (ok) {
           tc_fence_after();
           tmem_ld32(lane_base + (tg & 1) * L::TM_SBUF + 32 * wg, sreg);
           tmem_ld_wait32(sreg);
           const bool masked = (key0 + 32 > p.Skv) || (p.causal && key0 + 31 > it.qt * L::BM);
-          loc = masked ? fwd_scan_chunk<true>(sreg, key0, lim, c_t, c_a, slope2)
-                       : fwd_scan_chunk<false>(sreg, key0, lim, c_t, c_a, slope2);
+          loc = masked ? fwd_scan_chunk<true>(sreg, key0, lim, c_t, c_a, slope2, soff)
+                       : fwd_scan_chunk<false>(sreg, key0, lim, c_t, c_a, slope2, soff);
         }
         // exchange (chunk sigmoid total, chunk max of a') among the row's four warpgroups;
         // the barrier also orders every S read of this buffer before the P writes into it
@@ -474,8 +495,9 @@ __global__ void __launch_bounds__(640, 1)
           uint32_t preg[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
+            const float sh = shift + soff[j >> 2];  // keys 2j, 2j+1 lie in sub-chunk j / 4
             const float2 x = __fadd2_rn(make_float2(__uint_as_float(sreg[2 * j]), __uint_as_float(sreg[2 * j + 1])),
-                                        make_float2(-shift, -shift));
+                                        make_float2(-sh, -sh));
             // a quarter of the exponentials as a polynomial on the FMA pipe (measured best:
             // all on MUFU and half on the FMA pipe are both slower)
             const float2 e = ((j & 3) == 3) ? exp2_poly2(x) : make_float2(ex2_approx(x.x), ex2_approx(x.y));
