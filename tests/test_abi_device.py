@@ -148,7 +148,9 @@ def test_other_device_tensors_leave_current_device():
     t.join()
     assert seen == {"rc": 0, "ctx": None, "dev": 0}, seen
     torch.cuda.synchronize(1)
-    s0 = torch.cuda.current_stream(0).cuda_stream
-    assert lib.coalibi_fwd(ctypes.byref(fa), s0) == 9  # COALIBI_ERR_DEVICE
+    # a stream created on device 0 (the legacy default stream, handle 0, would mean
+    # "the default stream of the device being used" and is always accepted)
+    s0 = torch.cuda.Stream(device=0)
+    assert lib.coalibi_fwd(ctypes.byref(fa), s0.cuda_stream) == 9  # COALIBI_ERR_DEVICE
     assert "belongs to device 0" in lib.coalibi_last_error().decode()
     assert torch.cuda.current_device() == 0 and _current_ctx(drv) == ctx0
