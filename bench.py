@@ -791,18 +791,27 @@ def run_cp(args, world, rank, local_rank, dev):
             torch.empty_like(hosts[1]).pin_memory(), torch.empty_like(hosts[2]).pin_memory()]
     qd, kd, vd, dod = (torch.empty_like(x) for x in (q, k, v, do))
 
+    phase_events = []  # per e2e step: events before the copies in, after them, after the ring, after the copies out
+
     def e2e_step():
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        ev[0].record()
         for dst, src in zip((qd, kd, vd, dod), hosts):
             dst.copy_(src, non_blocking=True)
+        ev[1].record()
         qi, ki, vi = (x.detach().requires_grad_(True) for x in (qd, kd, vd))
         o = ring_attention(qi, ki, vi, causal=True, layout="zigzag")
         o.backward(dod)
+        ev[2].record()
         for dst, src in zip(outs, (o, qi.grad, ki.grad, vi.grad)):
             dst.copy_(src, non_blocking=True)
+        ev[3].record()
+        phase_events.append(ev)
 
     e2e_step()
     torch.cuda.synchronize()
     barrier()
+    phase_events.clear()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n_e2e = max(1, args.e2e_steps)
     f0.record()
@@ -810,10 +819,18 @@ def run_cp(args, world, rank, local_rank, dev):
         e2e_step()
     f1.record()
     torch.cuda.synchronize()
+    # where an e2e step's time goes on this rank (mean over the steps), then the max over ranks
+    phases = torch.tensor([sum(e[i].elapsed_time(e[i + 1]) for e in phase_events) / n_e2e for i in range(3)],
+                          device=dev)
     t = torch.tensor([f0.elapsed_time(f1) / n_e2e], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(phases, op=dist.ReduceOp.MAX)
     e2e_ms = t.item()
+    e2e_phases = {"h2d_ms": round(phases[0].item(), 3), "ring_fwd_bwd_ms": round(phases[1].item(), 3),
+                  "d2h_ms": round(phases[2].item(), 3),
+                  "note": "CUDA events on each rank's stream around its copies in, ring forward + backward and "
+                          "copies out, mean over the e2e steps, max over ranks"}
     burst, sustained, hbm, peak_src = load_peaks()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -842,7 +859,7 @@ def run_cp(args, world, rank, local_rank, dev):
             "cpu_baseline": cpu,
             "e2e": {"value": round(flops_step / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                     "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": sum(h.numel() * 2 for h in hosts),
-                    "d2h_bytes_per_step": sum(x.numel() * 2 for x in outs)},
+                    "d2h_bytes_per_step": sum(x.numel() * 2 for x in outs), "phases": e2e_phases},
             "gpu_launches": launches.get("fwd", 0) + 3 * launches.get("bwd_carry", 0),
             "clocks": clocks, "device_status": status,
         }
@@ -1016,30 +1033,46 @@ def main():
     torch.cuda.synchronize()
     assert co_alibi_attn.device_status(reset=True) == 0, "kernel-side error during warmup"
 
-    # ---------------- timed region (also records per-kernel events)
-    impl.kernel_events = {}
+    # ---------------- timed region: the public API alone, K steps back to back
     sampler = ClockSampler(physical_gpu_index(local_rank))
     sampler.start()
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
+    h0 = time.perf_counter()
     for _ in range(args.steps):
         step()
+    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps  # host time to enqueue a step
     e1.record()
     torch.cuda.synchronize()
     barrier()
     clocks = sampler.stop()
-    rec = impl.kernel_events
-    impl.kernel_events = None
     ms = e0.elapsed_time(e1) / args.steps
-    kern_ms = {name: statistics.mean(a.elapsed_time(b) for a, b in pairs) for name, pairs in rec.items()}
     status = co_alibi_attn.device_status(reset=True)
 
-    t = torch.tensor([ms], device=dev)
+    # ---------------- the same K steps again with CUDA events around every kernel launch
+    # (the backward then goes out as its three kernels, one C call each): per-kernel
+    # times for the breakdown and the roofline
+    impl.kernel_events = {}
+    barrier()
+    torch.cuda.synchronize()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record()
+    for _ in range(args.steps):
+        step()
+    g1.record()
+    torch.cuda.synchronize()
+    rec = impl.kernel_events
+    impl.kernel_events = None
+    ms_instr = g0.elapsed_time(g1) / args.steps
+    kern_ms = {name: statistics.mean(a.elapsed_time(b) for a, b in pairs) for name, pairs in rec.items()}
+    status = max(status, co_alibi_attn.device_status(reset=True))
+
+    t = torch.tensor([ms, host_ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = t.item()
+    ms_max, host_ms_max = t[0].item(), t[1].item()
     value = world * flops_step / (ms_max * 1e-3) / 1e12
 
     # ---------------- forward-only timing (the metric's fwd half)
@@ -1082,29 +1115,45 @@ def main():
 
     # ---------------- roofline of the dominant kernel
     burst, sustained, hbm, peak_src = load_peaks()
-    per_kernel_flops = {"fwd": 4.0 * D * E, "bwd_a": 6.0 * D * E, "bwd_b": 8.0 * D * E,
+    # which backward the library runs for this rank's problem: stored P / dS (pass B a
+    # streaming GEMM, 4 D per score, no MUFU) or recompute (pass B 8 D and the maths)
+    from co_alibi_attn import _lib as clib
+    lib = clib.load()
+    bargs = clib.CoalibiBwdArgs(B=B_r, Hq=Hq_r, Hkv=Hkv_r, Sq=S, Skv=S, D=D, causal=1 if causal else 0)
+    stored = lib.coalibi_bwd_workspace_size(bargs) != lib.coalibi_bwd_workspace_min_bytes(B_r, Hq_r, Hkv_r, S, S, D)
+    n_t = (S + 127) // 128
+    tiles = B_r * Hq_r * (n_t * (n_t + 1) // 2 if causal else n_t * n_t)
+    per_kernel_flops = {"fwd": 4.0 * D * E, "bwd_a": 6.0 * D * E, "bwd_b": (4.0 if stored else 8.0) * D * E,
                         "bwd_delta": 0.0}
     # MUFU ops per visible score: tanh sigmoid + exp2, less the quarter of the exp2
-    # that the forward and the D=128 pass B run as a polynomial on the FMA pipe
-    mufu_b = 1.75 if D == 128 else 2.0
+    # that the forward and the recompute path's D=128 pass B run as a polynomial on the FMA pipe
+    mufu_b = 0.0 if stored else (1.75 if D == 128 else 2.0)
     per_kernel_mufu = {"fwd": 1.75 * E, "bwd_a": 2.0 * E, "bwd_b": mufu_b * E, "bwd_delta": 0.0}
     dom = max(kern_ms, key=kern_ms.get)
     ach = per_kernel_flops[dom] / (kern_ms[dom] * 1e-3) / 1e12
     sm_mhz = clocks["sm_mhz"] if clocks else 1965.0
     kernels = {}
     for name, kms in kern_ms.items():
-        d = {"ms": round(kms, 4), "share": round(kms / ms, 4)}
+        d = {"ms": round(kms, 4), "share": round(kms / ms_instr, 4)}
         if per_kernel_flops[name]:
             d["tflops"] = round(per_kernel_flops[name] / (kms * 1e-3) / 1e12, 2)
             d["mufu_frac"] = round(per_kernel_mufu[name] / (16 * 148 * sm_mhz * 1e6 * kms * 1e-3), 4)
+        if name == "bwd_b" and stored:
+            # its bound: the P and dS tiles pass A wrote, read once from HBM (Q / dO re-reads hit L2)
+            pds = 2.0 * tiles * 128 * 128 * 2
+            d["pds_read_gbs"] = round(pds / (kms * 1e-3) / 1e9, 1)
+            d["hbm_frac"] = round(pds / (kms * 1e-3) / 1e9 / hbm, 4)
         kernels[name] = d
     roof = {"bound": "tensor", "kernel": dom, "achieved": round(ach, 2), "peak": burst, "unit": "TFLOP/s",
             "frac": round(ach / burst, 4), "peak_source": f"{peak_src} bf16_tflops (burst)",
             "traffic": NCU_TRAFFIC_CFG2.get(dom) if args.config == "cfg2" and B_r * Hkv_r == 8 * 16 else None,
             "flops_per_launch": per_kernel_flops[dom],
+            "backward_path": "stored P / dS" if stored else "recompute",
             "note": "algorithmic FLOPs on causal-visible scores of the kernel's GEMMs "
-                    "(fwd 4D, pass A 6D, pass B 8D per score) / mean CUDA-event duration in the timed region; "
-                    "second roofline: mufu_frac = MUFU ops per score (tanh + ex2 = 2, 1.75 where a quarter of the ex2 is a polynomial) / (16 ops/clk/SM x 148 SMs x sampled clock)"}
+                    "(fwd 4D, pass A 6D, pass B 4D stored path / 8D recompute path per score) / mean CUDA-event "
+                    "duration in the kernel-timing pass (the timed region's K steps repeated with events around "
+                    "each launch); second roofline: mufu_frac = MUFU ops per score (tanh + ex2 = 2, 1.75 where a "
+                    "quarter of the ex2 is a polynomial) / (16 ops/clk/SM x 148 SMs x sampled clock)"}
 
     verification = None
     if not args.no_verify:
@@ -1139,7 +1188,9 @@ def main():
             "fwd_bwd_tflops_reference_convention": round(
                 world * (12.0 * D * S * S * B_r * Hq_r if not fwd_only else 4.0 * D * S * S * B_r * Hq_r)
                 / (ms_max * 1e-3) / 1e12, 3),
-            "kernels": kernels, "roofline": roof, "cpu_baseline": cpu,
+            "host_enqueue_ms_per_step": round(host_ms_max, 4),
+            "kernels": kernels, "kernel_timing_pass_ms_per_step": round(ms_instr, 4),
+            "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": round(world * flops_step / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                     "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "copy_only_ms": round(copy_ms, 3),
