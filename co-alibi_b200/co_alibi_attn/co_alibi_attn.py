@@ -158,7 +158,11 @@ def _bwd(q, k, v, o, do, lse, rowsig, slopes, causal, sm_scale, dA_carry_in=None
     sigmoid total of the shard and of every key right of it.  The workspace is the
     library's preferred size for the problem (coalibi_bwd_workspace_size: P / dS
     stored by the first kernel while that stays below 24 GiB); ``min_workspace``
-    gives it the smallest size instead, which makes the backward recompute P / dS."""
+    (or COALIBI_BWD_WORKSPACE=min in the environment, for memory-tight callers) gives
+    it the smallest size instead, which makes the backward recompute P / dS in a
+    scratch of 8 bytes per row per 32 keys."""
+    if os.getenv("COALIBI_BWD_WORKSPACE", "") == "min":
+        min_workspace = True
     B, Hq, Sq, D = q.shape
     Hkv, Skv = k.shape[1], k.shape[2]
     lib = _lib.load()
