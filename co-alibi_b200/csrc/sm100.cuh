@@ -81,6 +81,20 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parit
   return ok != 0;
 }
 
+// try_wait with the hardware's own suspend limit (the thread resumes when the
+// phase completes or that limit passes).
+__device__ __forceinline__ bool mbar_try_wait_default(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Non-blocking probe (test_wait never suspends the thread, unlike try_wait).
 __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
@@ -94,17 +108,26 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+#ifndef COALIBI_WAIT_HINT_NS
+#define COALIBI_WAIT_HINT_NS 20
+#endif
+constexpr uint32_t kWaitHintNs = COALIBI_WAIT_HINT_NS;  // suspend-time hint of every mbarrier wait
+
 // Wait until the phase with the given parity has completed, polling with a
-// 20 ns suspend hint so the thread wakes within about that long of the phase
-// completing.  Returns false (and raises the CTA abort flag) when the wait
-// exceeds the guard's timeout or another role of the CTA has already aborted.
+// suspend hint of kWaitHintNs.  Returns false (and raises the CTA abort flag)
+// when the wait exceeds the guard's timeout or another role of the CTA has
+// already aborted.
+__device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity) {
+  return kWaitHintNs > 0 ? mbar_try_wait_hint(bar, parity, kWaitHintNs) : mbar_try_wait_default(bar, parity);
+}
+
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const CtaGuard& g) {
-  if (mbar_try_wait_hint(bar, parity, 20)) return true;
+  if (mbar_poll(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 64; ++i)
-      if (mbar_try_wait_hint(bar, parity, 20)) return true;
+      if (mbar_poll(bar, parity)) return true;
     if (g.aborted()) return false;
     if (global_timer_ns() - t0 > g.timeout_ns) {
       g.raise(kStatusTimeout);
