@@ -279,11 +279,10 @@ struct BwdALayout {
 // Per-key maths of pass A, two keys per packed f32x2 instruction (one issue
 // slot for two lanes of work; the softmax warps are issue-bound).
 //
-// Phase 1 of a 32-key chunk: sigmoids (kept in sg) and p*c_a - lse2 (kept in xa,
-// over the S registers); returns the chunk's sigmoid total.
+// Phase 1 of a 32-key chunk: sigmoids (kept in sg; the raw q.k values stay in
+// sreg); returns the chunk's sigmoid total.
 template <bool MASK>
-__device__ __forceinline__ float bwd_a_sig(uint32_t* sreg, float* sg, int key0, int lim, float c_t, float c_a,
-                                           float lse2) {
+__device__ __forceinline__ float bwd_a_sig(const uint32_t* sreg, float* sg, int key0, int lim, float c_t) {
   float2 tot = make_float2(0.f, 0.f);
 #pragma unroll
   for (int j = 0; j < 32; j += 2) {
@@ -296,28 +295,27 @@ __device__ __forceinline__ float bwd_a_sig(uint32_t* sreg, float* sg, int key0, 
     sg[j] = sv.x;
     sg[j + 1] = sv.y;
     tot = __fadd2_rn(tot, sv);
-    const float2 xa = __ffma2_rn(x, make_float2(c_a, c_a), make_float2(-lse2, -lse2));
-    sreg[j] = __float_as_uint(xa.x);
-    sreg[j + 1] = __float_as_uint(xa.y);
   }
   return tot.x + tot.y;
 }
 
-// Phase 2 on 16 keys: P from the sigmoid suffix zz, dA = P (dP - delta) over the
-// xa registers; returns the sum of dA.  With STORE, also P packed to 16 bits in pk.
+// Phase 2 on 16 keys: P = 2^(c_a x + Z) with the sigmoid suffix carried in
+// exponent units, Z = -lse2 - slope2 * z (so each key adds slope2 * s to it and the
+// exponent is one FMA of the raw q.k value x), dA = P (dP - delta) over the x
+// registers; returns the sum of dA.  With STORE, also P packed to 16 bits in pk.
 template <bool MASK, bool BF16, bool STORE>
 __device__ __forceinline__ float bwd_a_da(uint32_t* xa, const float* sg, const uint32_t* dpr, int key0, int lim,
-                                          float slope2, float delta, float& zz, uint32_t* pk) {
+                                          float c_a, float slope2, float delta, float& zz, uint32_t* pk) {
   float2 tot = make_float2(0.f, 0.f);
 #pragma unroll
   for (int j = 0; j < 16; j += 2) {
     float2 z;
     z.x = zz;
-    zz -= sg[j];
+    zz = fmaf(slope2, sg[j], zz);
     z.y = zz;
-    zz -= sg[j + 1];
-    const float2 e = __ffma2_rn(make_float2(-slope2, -slope2), z,
-                                make_float2(__uint_as_float(xa[j]), __uint_as_float(xa[j + 1])));
+    zz = fmaf(slope2, sg[j + 1], zz);
+    const float2 e = __ffma2_rn(make_float2(__uint_as_float(xa[j]), __uint_as_float(xa[j + 1])),
+                                make_float2(c_a, c_a), z);
     float2 P;
     P.x = ex2_approx(e.x);
     P.y = ex2_approx(e.y);
@@ -582,8 +580,7 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(s_free);
-        tot = masked ? bwd_a_sig<true>(xa, sg, key0, lim, c_t, c_a, lse2)
-                     : bwd_a_sig<false>(xa, sg, key0, lim, c_t, c_a, lse2);
+        tot = masked ? bwd_a_sig<true>(xa, sg, key0, lim, c_t) : bwd_a_sig<false>(xa, sg, key0, lim, c_t);
       }
       // sigmoid suffix sum at this chunk's first key, from the warpgroup to the left
       // (warpgroup 0: from warpgroup 3's previous sub-tile)
@@ -598,7 +595,7 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
         xs[nwg * 128 + t_row] = z0 - tot;
         mbar_arrive(&zlink[quarter * L::NWG + nwg]);
       }
-      float zz = z0;
+      float zz = fmaf(-slope2, z0, -lse2);  // the suffix in exponent units (bwd_a_da)
       ok = mbar_wait(dp_full, n & 1, g);
       ok = __all_sync(0xffffffffu, ok);
       float dtot = 0.f;
@@ -615,10 +612,10 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
             if (lane == 0) mbar_arrive(dp_free);
           }
           uint32_t pk[8];
-          dtot += masked ? bwd_a_da<true, BF16, STORE>(xa + 16 * hh, sg + 16 * hh, dpr, key0 + 16 * hh, lim, slope2,
-                                                       delta, zz, pk)
-                         : bwd_a_da<false, BF16, STORE>(xa + 16 * hh, sg + 16 * hh, dpr, key0 + 16 * hh, lim, slope2,
-                                                        delta, zz, pk);
+          dtot += masked ? bwd_a_da<true, BF16, STORE>(xa + 16 * hh, sg + 16 * hh, dpr, key0 + 16 * hh, lim, c_a,
+                                                       slope2, delta, zz, pk)
+                         : bwd_a_da<false, BF16, STORE>(xa + 16 * hh, sg + 16 * hh, dpr, key0 + 16 * hh, lim, c_a,
+                                                        slope2, delta, zz, pk);
           if (STORE) {
             uint16_t* dst = pd_row + n * (2 * 128 * 128) + (2 * hh) * 1024;
             st_global_na(dst, make_uint4(pk[0], pk[1], pk[2], pk[3]));
