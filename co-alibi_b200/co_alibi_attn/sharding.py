@@ -8,7 +8,7 @@ from dataclasses import dataclass
 
 import torch
 
-from .co_alibi_attn import CoALIBIAttention, _get_coalibi_slopes
+from .co_alibi_attn import CoALIBIAttention, _api_slopes
 
 
 @dataclass(frozen=True)
@@ -49,9 +49,11 @@ def shard_plan(B: int, Hq: int, Hkv: int, world: int, rank: int) -> Shard:
 
 
 def shard_slopes(Hq: int, shard: Shard, bias_max: float, dtype, device) -> torch.Tensor:
-    """The API's slope tensor (2 * table, cast to dtype) restricted to the shard's query heads."""
-    full = (2.0 * _get_coalibi_slopes(Hq, bias_max)).to(device, dtype=dtype)
-    return full[shard.h0:shard.h1].contiguous()
+    """The API's slope tensor (2 * table, cast to dtype) restricted to the shard's query
+    heads: a view into the device table the API caches per (Hq, bias_max, dtype, device),
+    so a call copies nothing from the host (a pageable host-to-device copy would wait
+    for the stream to drain and stall every step's launches behind the previous step)."""
+    return _api_slopes(Hq, bias_max, dtype, device)[shard.h0:shard.h1]
 
 
 def sharded_attention(q, k, v, shard: Shard, Hq: int, causal=True, sm_scale=None, bias_max=8.0):
