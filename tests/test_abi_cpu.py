@@ -136,3 +136,14 @@ def test_sharded_api_slopes_are_global():
     sh = shard_plan(4, 32, 8, 8, 5)
     s = shard_slopes(32, sh, 8.0, torch.float32, "cpu")
     assert torch.equal(s, (2.0 * _get_coalibi_slopes(32, 8.0))[20:24].float())
+
+
+def test_sharded_slopes_are_views_of_the_cached_table():
+    # no per-call host-to-device copy: every call returns a view into one cached table
+    from co_alibi_attn.sharding import shard_plan, shard_slopes
+    sh = shard_plan(4, 32, 8, 8, 5)
+    a = shard_slopes(32, sh, 8.0, torch.float32, "cpu")
+    b = shard_slopes(32, sh, 8.0, torch.float32, "cpu")
+    assert a.is_contiguous() and a.shape == (4,)
+    assert a.data_ptr() == b.data_ptr()
+    assert a.untyped_storage().data_ptr() == b.untyped_storage().data_ptr()
