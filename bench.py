@@ -57,7 +57,7 @@ CONFIGS = {
 # kernel at cfg2: one ncu capture at B=2 (profiles/<kernel>_kernel_cfg2_b2_ncu_full.txt)
 # scaled by 4 to the B=8 launch (traffic grows with the number of (b, h) units).
 # Pass A and pass B are the stored path's (pass A writes the P / dS tiles pass B reads).
-NCU_TRAFFIC_CFG2 = {"fwd": 4 * 116.65e6, "bwd_a": 4 * 1228.1e6, "bwd_b": 4 * 1241.5e6, "bwd_delta": None}
+NCU_TRAFFIC_CFG2 = {"fwd": 4 * 117.26e6, "bwd_a": 4 * 1229.95e6, "bwd_b": 4 * 1244.0e6, "bwd_delta": None}
 
 
 def visible(S, causal):
