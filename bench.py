@@ -487,7 +487,8 @@ def run_reference_arm(args, cfg, rank):
                          "sample": desc},
         "e2e": {"value": round(tfl, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference arm: the reference's own CPU path (model.py maths) restated in oracle/, "
-                "timed on the host cores; the reference's Triton GPU kernels are not installable here",
+                "timed on the host cores; the reference's Triton GPU kernels are timed on the same GPU by "
+                "the default arm (its reference_triton key, from baseline/_ref when installed)",
     }
     print(json.dumps(line), flush=True)
 
