@@ -156,6 +156,8 @@ __global__ void __launch_bounds__(256) coalibi_bwd_delta_kernel(const BwdParams 
   const int sub = lane % LPR;
   float acc = 0.f;
   int bh = 0, row = 0;
+  grid_dep_wait();  // before any global-memory access
+  grid_dep_launch();
   if (rg < nrows) {
     bh = (int)(rg / p.sq_pad);
     row = (int)(rg - (long long)bh * p.sq_pad);
@@ -410,6 +412,8 @@ __global__ void __launch_bounds__(BwdALayout<D>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dep_wait();  // before any global-memory access
+  grid_dep_launch();
 
   if (warp >= L::WARP_TMA) {
     regs_decrease<STORE ? L::REGS_PRODUCER_ST : L::REGS_PRODUCER>();
@@ -827,6 +831,8 @@ __global__ void __launch_bounds__(BwdBLayout<D>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dep_wait();  // before any global-memory access
+  grid_dep_launch();
 
   if (warp == L::WARP_TMA) {
     if (lane == 0 && NIT > 0) {
@@ -1283,6 +1289,8 @@ __global__ void __launch_bounds__(BwdB128Layout::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dep_wait();  // before any global-memory access
+  grid_dep_launch();
 
   if (warp >= L::WARP_TMA) {
     regs_decrease<L::REGS_PRODUCER>();
@@ -1655,6 +1663,8 @@ __global__ void __launch_bounds__(BwdKVLayout<D>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dep_wait();  // before any global-memory access
+  grid_dep_launch();
 
   if (warp == L::WARP_TMA) {
     if (lane == 0 && NSTEP > 0) {
@@ -1843,26 +1853,32 @@ inline int bwd_launch_t(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigne
   }
 
   const long long rows = (long long)a.B * a.Hq * p.sq_pad;
+  cudaError_t e = cudaSuccess;
+  auto keep = [&e](cudaError_t r) {
+    if (e == cudaSuccess) e = r;
+  };
   if (phases & 1)
-    coalibi_bwd_delta_kernel<D, BF16><<<(unsigned)((rows + 8 * (256 / D) - 1) / (8 * (256 / D))), 256, 0, stream>>>(p);
+    keep(launch_pdl(coalibi_bwd_delta_kernel<D, BF16>, dim3((unsigned)((rows + 8 * (256 / D) - 1) / (8 * (256 / D)))),
+                    dim3(256), 0, stream, p));
   if ((phases & 2) && ws.stored)
-    coalibi_bwd_a_kernel<D, BF16, true><<<a.B * a.Hq * p.n_qtiles, BwdALayout<D>::THREADS, BwdALayout<D>::ALLOC,
-                                          stream>>>(tq, tdo, tk, tv, p);
+    keep(launch_pdl(coalibi_bwd_a_kernel<D, BF16, true>, dim3(a.B * a.Hq * p.n_qtiles), dim3(BwdALayout<D>::THREADS),
+                    BwdALayout<D>::ALLOC, stream, tq, tdo, tk, tv, p));
   if ((phases & 2) && !ws.stored)
-    coalibi_bwd_a_kernel<D, BF16, false><<<a.B * a.Hq * p.n_qtiles, BwdALayout<D>::THREADS, BwdALayout<D>::ALLOC,
-                                           stream>>>(tq, tdo, tk, tv, p);
+    keep(launch_pdl(coalibi_bwd_a_kernel<D, BF16, false>, dim3(a.B * a.Hq * p.n_qtiles), dim3(BwdALayout<D>::THREADS),
+                    BwdALayout<D>::ALLOC, stream, tq, tdo, tk, tv, p));
   if ((phases & 4) && ws.stored) {
-    coalibi_bwd_kv_kernel<D, BF16><<<a.B * a.Hkv * p.n_kvtiles, BwdKVLayout<D>::THREADS, BwdKVLayout<D>::ALLOC,
-                                     stream>>>(tq, tdo, p);
+    keep(launch_pdl(coalibi_bwd_kv_kernel<D, BF16>, dim3(a.B * a.Hkv * p.n_kvtiles), dim3(BwdKVLayout<D>::THREADS),
+                    BwdKVLayout<D>::ALLOC, stream, tq, tdo, p));
   } else if (phases & 4) {
     if constexpr (D == 128)
-      coalibi_bwd_b128_kernel<BF16>
-          <<<a.B * a.Hkv * p.n_blocks, BwdB128Layout::THREADS, BwdB128Layout::ALLOC, stream>>>(tq, tdo, tkb, tvb, p);
+      keep(launch_pdl(coalibi_bwd_b128_kernel<BF16>, dim3(a.B * a.Hkv * p.n_blocks), dim3(BwdB128Layout::THREADS),
+                      BwdB128Layout::ALLOC, stream, tq, tdo, tkb, tvb, p));
     else
-      coalibi_bwd_b_kernel<D, BF16>
-          <<<a.B * a.Hkv * p.n_blocks, BwdBLayout<D>::THREADS, BwdBLayout<D>::ALLOC, stream>>>(tq, tdo, tkb, tvb, p);
+      keep(launch_pdl(coalibi_bwd_b_kernel<D, BF16>, dim3(a.B * a.Hkv * p.n_blocks), dim3(BwdBLayout<D>::THREADS),
+                      BwdBLayout<D>::ALLOC, stream, tq, tdo, tkb, tvb, p));
   }
-  return cudaGetLastError() == cudaSuccess ? COALIBI_OK : COALIBI_ERR_LAUNCH;
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e == cudaSuccess ? COALIBI_OK : COALIBI_ERR_LAUNCH;
 }
 
 inline int bwd_launch(const CoalibiBwdArgs& a, const BwdWorkspace& ws, unsigned long long tmo,

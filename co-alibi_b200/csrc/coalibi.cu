@@ -279,8 +279,9 @@ int launch_fwd_impl(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensor
   const int n_items = p.B * p.Hq * p.n_qtiles;
   const int sms = current_sm_count();
   const int grid = (n_items >= 12 * sms) ? sms : n_items;
-  coalibi_fwd_kernel<D, BF16><<<grid, FwdLayout<D>::THREADS, FwdLayout<D>::ALLOC, stream>>>(tq, tk, tv, p);
-  const cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(coalibi_fwd_kernel<D, BF16>, dim3(grid), dim3(FwdLayout<D>::THREADS), FwdLayout<D>::ALLOC,
+                             stream, tq, tk, tv, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     snprintf(g_last_error, sizeof(g_last_error), "forward launch: %s", cudaGetErrorString(e));
     return COALIBI_ERR_LAUNCH;

@@ -272,6 +272,8 @@ __global__ void __launch_bounds__(640, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dep_wait();  // before any global-memory access
+  grid_dep_launch();
 
   if (warp >= 16) {
     regs_decrease<L::REGS_PRODUCER>();

@@ -8,8 +8,10 @@
 #pragma once
 
 #include <cstdint>
+#include <utility>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
+#include <cuda_runtime.h>
 
 namespace coalibi {
 
@@ -29,6 +31,41 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
+
+// ----------------------------------------------------------------------------
+// Programmatic dependent launch.  The attention kernels are launched with the
+// programmatic-stream-serialization attribute, so a kernel's CTAs may start (and
+// run their set-up: barrier init, TMEM allocation) while the kernel before it on
+// the stream is still finishing.  grid_dep_wait() blocks until every grid this
+// one depends on has completed and its memory operations are visible (it returns
+// at once for a launch without the attribute), and every kernel calls it before
+// its first global-memory access.  grid_dep_launch() comes after that wait: it
+// lets the next such launch begin, and since by then this grid's own
+// predecessors have completed, ordering stays transitive along the stream.
+// ----------------------------------------------------------------------------
+#ifndef COALIBI_PDL
+#define COALIBI_PDL 1
+#endif
+
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launch `kernel` on `stream` with programmatic stream serialization allowed.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = COALIBI_PDL ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ----------------------------------------------------------------------------
 // Abort / status plumbing shared by all roles of a CTA.

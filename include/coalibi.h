@@ -23,6 +23,11 @@
  * streams and devices.  Each function returns COALIBI_OK or an error code;
  * coalibi_strerror() names it.  Kernel-side failures (a bounded wait that timed
  * out) are reported asynchronously through the optional device status word.
+ *
+ * The forward and backward kernels are launched with programmatic stream
+ * serialization: one may start its set-up while the kernel before it on the
+ * stream is still finishing, but it waits for that kernel to complete before
+ * it touches global memory, so stream order holds for every read and write.
  */
 #ifndef COALIBI_H_
 #define COALIBI_H_
