@@ -27,6 +27,7 @@ CASES = [
     (1, 3, 3, 384, 384, 64, False, torch.float16),
     (2, 4, 4, 1024, 1024, 128, True, torch.float16),
     (1, 12, 12, 513, 513, 64, True, torch.bfloat16),
+    (1, 8, 2, 333, 333, 64, False, torch.bfloat16),
 ]
 
 
