@@ -79,7 +79,9 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc, boo
                : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all_but_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+// Wait until at most N of this thread's most recent cp.async groups are still pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait_pending() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------
@@ -126,7 +128,11 @@ struct DecodeMmaSmem {
   static constexpr int NT = STEP / 8;        // 8-key n-tiles of S per step
   static constexpr int ROW = D * 2 + 16;     // padded rows: the 8 rows of an ldmatrix hit distinct banks
   static constexpr int TILE = STEP * ROW;    // one K or V step tile
-  static constexpr int PER_WARP = 4 * TILE;  // K and V, two buffers each
+#ifndef COALIBI_DECODE_STAGES
+#define COALIBI_DECODE_STAGES 3
+#endif
+  static constexpr int NBUF = COALIBI_DECODE_STAGES;  // per-warp ring of K/V steps: NBUF - 1 steps in flight
+  static constexpr int PER_WARP = 2 * NBUF * TILE;    // K and V, NBUF buffers each
   static constexpr int BYTES = 4 * PER_WARP;
 };
 
@@ -187,7 +193,7 @@ __global__ void __launch_bounds__(128) coalibi_decode_mma_kernel(const DecodePar
   const int nsteps = hi > lo ? (hi - lo + S::STEP - 1) / S::STEP : 0;
   auto stage = [&](int st) {
     const int kb = lo + st * S::STEP;
-    uint8_t* kt = wbase + (st & 1) * 2 * S::TILE;
+    uint8_t* kt = wbase + (st % S::NBUF) * 2 * S::TILE;
     uint8_t* vt = kt + S::TILE;
 #pragma unroll
     for (int it = 0; it < S::STEP * (D / 8) / 32; ++it) {
@@ -199,16 +205,20 @@ __global__ void __launch_bounds__(128) coalibi_decode_mma_kernel(const DecodePar
       cp_async16(vt + key * S::ROW + pc * 16, static_cast<const uint16_t*>(p.v) + off, ok);
     }
   };
-  if (nsteps > 0) stage(nsteps - 1);
-  cp_async_commit();
+  // one cp.async group per step (empty past the last one), NBUF - 1 steps ahead of the one computed
+#pragma unroll
+  for (int a = 1; a < S::NBUF; ++a) {
+    if (nsteps - a >= 0) stage(nsteps - a);
+    cp_async_commit();
+  }
   const int mat = lane >> 3, row8 = lane & 7;
   for (int st = nsteps - 1; st >= 0; --st) {
-    if (st > 0) stage(st - 1);
+    if (st - (S::NBUF - 1) >= 0) stage(st - (S::NBUF - 1));
     cp_async_commit();
-    cp_async_wait_all_but_one();
+    cp_async_wait_pending<S::NBUF - 1>();  // the group of step st has landed
     __syncwarp();
     const int kb = lo + st * S::STEP;
-    const uint32_t kt = smem_u32(wbase + (st & 1) * 2 * S::TILE);
+    const uint32_t kt = smem_u32(wbase + (st % S::NBUF) * 2 * S::TILE);
     const uint32_t vt = kt + S::TILE;
     // ---- S = Q K^T: n-tile nt holds keys 8nt .. 8nt+7 of the step
     float sc[NT][4];
